@@ -1,0 +1,59 @@
+// tcgen05 GEMM: host-side plan / launch interface.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace cn {
+
+enum Epi : int {
+  EPI_F32_ACCUM = 0,  // C[m][n] += acc                       (WMMA semantics D = C + A*B)
+  EPI_F16 = 1,        // out16[m][n] = f16(act(acc + bias[n]))  (+ optional f32 copy)
+  EPI_RESID = 2,      // x32[m][n] += acc + bias[n]
+  EPI_TOKENS = 3,     // x32[row(m)][n] = ((acc + bias[n]) + pos[t][n]) + cond[clip][n]
+  EPI_F32_OUT = 4,    // out32[m][n] = acc + bias[n]
+};
+enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2, ACT_TANH = 3 };
+
+struct GemmParams {
+  int M, N, K;        // per group; K % 64 == 0
+  int splits;         // split-K factor == cluster size along z
+  int epi, act;
+  void* out;          // f16 (EPI_F16) or f32 base
+  long long ldo;      // out row stride (elements)
+  long long out_gstride;  // elements between groups
+  const float* bias;  // [G][N] (group stride = bias_gstride) or nullptr
+  long long bias_gstride;
+  float* out32;       // EPI_F16: optional f32 copy of the rounded value
+  long long ld32;
+  // EPI_TOKENS row mapping: GEMM row m of group g -> clip = m / rows_per_clip,
+  // token t = tok_base + g * tok_gstride + m % rows_per_clip,
+  // residual row = clip * T + t.
+  const float* pos;   // [T][N]
+  const float* cond;  // [clips][cond_ld]
+  long long cond_ld;
+  int rows_per_clip, tok_base, tok_gstride, T;
+};
+
+struct GemmPlan {
+  CUtensorMap ta, tb;
+  GemmParams p;
+  dim3 grid;
+  int bn;
+  bool b_mn;
+  size_t smem;
+};
+
+// A: [G][M][K] f16, row stride lda (elements), group stride a_gs (elements).
+// B: K-major [G][N][K] (row stride ldb) or, with b_mn, MN-major [G][K][N].
+// bn/splits <= 0 pick a tiling automatically.  Returns 0 or a cudaError_t /
+// CUresult code (also recorded in the engine's last-error string).
+int gemm_plan(GemmPlan* g, const void* A, long long lda, long long a_gs, const void* B, long long ldb,
+              long long b_gs, int M, int N, int K, int G, bool b_mn, int bn, int splits, const GemmParams& epi);
+int gemm_launch(const GemmPlan& g, cudaStream_t stream);
+int gemm_choose(int M, int N, int K, int G, int* bn, int* splits);
+
+int device_error_read_and_clear(cudaStream_t stream, int* code);
+const char* last_error_text();
+void set_last_error(const char* fmt, ...);
+
+}  // namespace cn

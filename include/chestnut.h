@@ -1,0 +1,144 @@
+/* chestnut.h -- C ABI of the B200 chestnut frame engine (libchestnut.so).
+ *
+ * Every entry point returns 0 on success or a nonzero status; it never aborts
+ * and never throws.  cn_last_error() returns a thread-local description of the
+ * last failure.  Host pointers are owned by the caller; device buffers are
+ * owned by the engine.  An engine is bound to one device and must be driven by
+ * one host thread at a time (the reference's run_frame is likewise not
+ * re-entrant: run_pinned2.py:1462-1463 uses module globals).
+ *
+ * Reference interfaces replaced (Alice7371/chestnut-on-pc):
+ *   cn_engine_create   <- model load + recompile + queue allocation,
+ *                         run_pinned2.py:1346-1389
+ *   cn_run_frame       <- run_frame(warped_np, packed), run_pinned2.py:1462-1565
+ *   cn_run_frames      <- the video_check.py:50-66 loop with hidden-state carry
+ *   cn_get_state /
+ *   cn_set_state       <- the module-level queues dict, run_pinned2.py:1379-1386
+ *   cn_kernel_list     <- _LIN_BY_NAME / the recorded 497-launch plan,
+ *                         run_pinned2.py:1092, :1472-1474
+ *   cn_output_slices   <- meta['output_slices'], run_pinned2.py:1355
+ *   cn_gemm_wmma_f16   <- the RDNA4 WMMA attention GEMM r_6_2_32_4_2_2_2_4_4_384
+ *                         (run_pinned2.py:100-269; bench_r62.py:13-15)
+ *   cn_reduce_rows_f16 <- the serial reduce r_32_32_3_12288_32 and its warp
+ *                         split (run_pinned2.py:989-1066; bench_alu.py:13-16)
+ *   cn_border_gather_s2<- the image2d zero-border read (run_pinned2.py:56-92,
+ *                         :690-716)
+ */
+#ifndef CHESTNUT_H
+#define CHESTNUT_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CN_OK 0
+#define CN_ERR_ARG (-2)
+#define CN_ERR_CUDA (-3)
+#define CN_ERR_DEVICE (-4)  /* a kernel recorded a device-side error (bounded wait expired) */
+#define CN_ERR_STATE (-5)
+
+#define CN_MODEL_39M 0
+#define CN_MODEL_1B 1
+
+#define CN_FRAME_BYTES (2 * 6 * 128 * 256)  /* warped u8[2,6,128,256] per clip */
+#define CN_PACKED 524                      /* desire8 | tc2 | action_t2 | prev_feat512 */
+#define CN_N_OUT 3323                      /* plan 2475 | lane_lines 264 | lead 72 | hidden_state 512 */
+
+typedef struct cn_engine cn_engine;
+
+typedef struct cn_config {
+  int model;          /* CN_MODEL_39M or CN_MODEL_1B */
+  int device;         /* CUDA device ordinal */
+  int batch;          /* clips per launch (independent recurrent states) */
+  int use_graph;      /* 1: replay the frame as one CUDA graph; 0: eager launches */
+  int carry_hidden;   /* 1: feed hidden_state back on the device (packed[12:] ignored) */
+  uint64_t seed;      /* weight seed (hash RNG), < 2^16 */
+} cn_config;
+
+typedef struct cn_kernel_info {
+  char name[64];
+  unsigned grid[3];
+  unsigned block[3];
+  unsigned cluster[3];
+  unsigned smem_bytes;
+} cn_kernel_info;
+
+typedef struct cn_slice {
+  char name[16];
+  int start, stop;
+} cn_slice;
+
+const char* cn_last_error(void);
+int cn_version(void);
+
+/* ---- frame engine ---------------------------------------------------- */
+int cn_engine_create(const cn_config* cfg, cn_engine** out);
+int cn_engine_destroy(cn_engine* e);
+/* warped: host u8 [batch][2][6][128][256]; packed: host f32 [batch][524];
+ * out: host f32 [batch][CN_N_OUT] or NULL (the frame is then left in flight
+ * and its output on the device; read it with cn_read_output). */
+int cn_run_frame(cn_engine* e, const uint8_t* warped, const float* packed, float* out);
+/* n frames back to back with the hidden state carried by the caller's rule
+ * packed[12:] = out[hidden_state] (video_check.py:60); outs: [n][batch][N_OUT]. */
+int cn_run_frames(cn_engine* e, int n, const uint8_t* warped, const float* packed0, float* outs);
+/* Same frame with inputs already resident on the device (d_warped, d_packed
+ * device pointers in the layouts above); output stays on the device. */
+int cn_run_frame_device(cn_engine* e, const void* d_warped, const void* d_packed);
+int cn_read_output(cn_engine* e, float* out);
+int cn_sync(cn_engine* e);
+/* Canonical queue state of one clip: img_q u8[5,6,128,256] | big_img_q
+ * u8[5,6,128,256] | feat_q f32[96,512] | desire_q f32[100,8] |
+ * hidden f32[512] (the device-carried prev_feat). */
+size_t cn_state_bytes(void);
+int cn_get_state(cn_engine* e, int clip, void* buf, size_t bytes);
+int cn_set_state(cn_engine* e, int clip, const void* buf, size_t bytes);
+int cn_kernel_list(cn_engine* e, cn_kernel_info* out, int* n_inout);
+/* Eager run of one frame with an event pair around every launch; ms[i] is
+ * the duration of kernel i of cn_kernel_list. */
+int cn_profile_frame(cn_engine* e, const uint8_t* warped, const float* packed, float* ms, int* n_inout);
+/* Per-launch durations of the marked kernel class inside the last graph
+ * replay (see cn_set_timed_class); returns the count in *n. */
+int cn_set_timed_class(cn_engine* e, const char* name_prefix);
+int cn_timed_class_ms(cn_engine* e, float* ms, int* n_inout);
+int cn_engine_info(cn_engine* e, long long* n_params, long long* weight_bytes, int* n_kernels);
+
+/* ---- model description (host only, no GPU needed) ---------------------- */
+int cn_output_slices(cn_slice* out, int* n_inout);
+int cn_param_count(int model);
+int cn_param_info(int model, int index, char* name, int name_len, int* tensor_id, long long* rows,
+                  long long* cols, long long* valid_cols, int* kind);
+
+/* ---- kernel-level entry points (device pointers, caller's stream) ------ */
+/* C[M][N] += A[M][K] * B, f16 inputs, f32 accumulate (WMMA D = C + A*B).
+ * b_kmajor: 1 -> B is [N][K]; 0 -> B is [K][N].  K % 64 == 0.
+ * bn / splits <= 0 choose a tiling automatically. */
+int cn_gemm_wmma_f16(const void* A, const void* B, float* C, int M, int N, int K, int b_kmajor, int bn,
+                     int splits, void* stream);
+/* out[r] = sum_i x[r][i] * w[i]; x f16 [rows][len], w f16 [len]; f32 out.
+ * chunks_per_row in {1,2,4,8} (0 = automatic). */
+int cn_reduce_rows_f16(const void* x, const void* w, float* out, long long rows, long long len, int chunks_per_row,
+                       void* stream);
+/* 3x3 / stride-2 / pad-1 zero-border gather of NHWC f16 [G][B][H][W][C] into
+ * f16 [G][B*(H/2)*(W/2)][9*C], k = tap*C + c; C % 8 == 0. */
+int cn_border_gather_s2(const void* act, int G, int B, int H, int W, int C, void* out, void* stream);
+/* Read (and clear) the device error word. */
+int cn_device_error(int* code);
+
+/* ---- plumbing for hosts without a CUDA binding (ctypes callers) ------- */
+int cn_dev_alloc(void** ptr, size_t bytes, int device);
+int cn_dev_free(void* ptr);
+int cn_host_alloc_pinned(void** ptr, size_t bytes);
+int cn_host_free_pinned(void* ptr);
+/* kind: 0 host->device, 1 device->host, 2 device->device (synchronous) */
+int cn_memcpy(void* dst, const void* src, size_t bytes, int kind);
+int cn_memset(void* dst, int value, size_t bytes);
+int cn_device_synchronize(int device);
+int cn_engine_stream(cn_engine* e, void** stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CHESTNUT_H */
