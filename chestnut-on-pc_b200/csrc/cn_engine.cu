@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstring>
 #include <functional>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -431,7 +432,7 @@ static int build_plan(cn_engine* e) {
       const int hd = d / H;
       const size_t smem = (size_t)(hd * 96 * 2 + 8 * hd + 8 * 96) * 4;
       e->steps.push_back({"attn", [q, o, B, d, H](cudaStream_t s) { return launch_attention(q, o, B, kT, d, H, s); },
-                          kinfo(("attention:" + pre).c_str(), dim3(B * H), dim3(256), dim3(1, 1, 1), smem)});
+                          kinfo(("attention:" + pre).c_str(), dim3(B * H, (kT + 7) / 8), dim3(256), dim3(1, 1, 1), smem)});
     }
     {
       GemmParams ep;
@@ -466,7 +467,7 @@ static int build_plan(cn_engine* e) {
     __half* p = e->pooled;
     const int d = m.d;
     e->steps.push_back({"pool", [x, p, B, d](cudaStream_t s) { return launch_pool(x, p, B, kT, d, s); },
-                        kinfo("ln_mean_pool", dim3(B), dim3(256), dim3(1, 1, 1), 0)});
+                        kinfo("ln_mean_pool", dim3(B, d / 128), dim3(128), dim3(1, 1, 1), 0)});
   }
   {
     GemmParams ep = epi_f16(e->hid16, kFeat, 0, (const float*)wptr(e, "hid.b"), 0, ACT_TANH);
@@ -496,14 +497,15 @@ static int run_steps(cn_engine* e, cudaStream_t s, bool with_events) {
   size_t ev = 0;
   for (auto& st : e->steps) {
     const bool t = with_events && timed(e, st);
-    if (t) CN_CUDA(cudaEventRecord(e->tev[ev], s));
+    // External records become real event-record nodes when captured into the graph.
+    if (t) CN_CUDA(cudaEventRecordWithFlags(e->tev[ev], s, cudaEventRecordExternal));
     int r = st.fn(s);
     if (r) {
       if (r > 0) set_last_error("launch of %s failed: %s", st.info.name, cudaGetErrorString((cudaError_t)r));
       return r < 0 ? r : CN_ERR_CUDA;
     }
     if (t) {
-      CN_CUDA(cudaEventRecord(e->tev[ev + 1], s));
+      CN_CUDA(cudaEventRecordWithFlags(e->tev[ev + 1], s, cudaEventRecordExternal));
       ev += 2;
     }
   }
@@ -857,16 +859,49 @@ int cn_gemm_wmma_f16(const void* A, const void* B, float* C, int M, int N, int K
     set_last_error("cn_gemm_wmma_f16: null pointer");
     return CN_ERR_ARG;
   }
-  GemmParams ep;
-  memset(&ep, 0, sizeof(ep));
-  ep.epi = EPI_F32_ACCUM;
-  ep.out = C;
-  ep.ldo = N;
+  struct Key {
+    const void *a, *b;
+    float* c;
+    int m, n, k, kmaj, bn, s, dev;
+    bool operator==(const Key& o) const {
+      return a == o.a && b == o.b && c == o.c && m == o.m && n == o.n && k == o.k && kmaj == o.kmaj && bn == o.bn &&
+             s == o.s && dev == o.dev;
+    }
+  };
+  static std::mutex mu;
+  static Key keys[16];
+  static GemmPlan plans[16];
+  static int used = 0, next = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const Key key{A, B, C, M, N, K, b_kmajor, bn, splits, dev};
   GemmPlan g;
-  const bool mn = !b_kmajor;
-  int r = gemm_plan(&g, A, K, 0, B, mn ? N : K, 0, M, N, K, 1, mn, bn, splits, ep);
-  if (r) return r < 0 ? r : CN_ERR_CUDA;
-  r = gemm_launch(g, (cudaStream_t)stream);
+  bool hit = false;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < used; ++i)
+      if (keys[i] == key) {
+        g = plans[i];
+        hit = true;
+        break;
+      }
+  }
+  if (!hit) {
+    GemmParams ep;
+    memset(&ep, 0, sizeof(ep));
+    ep.epi = EPI_F32_ACCUM;
+    ep.out = C;
+    ep.ldo = N;
+    const bool mn = !b_kmajor;
+    int r = gemm_plan(&g, A, K, 0, B, mn ? N : K, 0, M, N, K, 1, mn, bn, splits, ep);
+    if (r) return r < 0 ? r : CN_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(mu);
+    keys[next] = key;
+    plans[next] = g;
+    next = (next + 1) % 16;
+    if (used < 16) ++used;
+  }
+  int r = gemm_launch(g, (cudaStream_t)stream);
   return r ? (r < 0 ? r : CN_ERR_CUDA) : 0;
 }
 

@@ -15,8 +15,10 @@ enum Epi : int {
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2, ACT_TANH = 3 };
 
 struct GemmParams {
-  int M, N, K;        // per group; K % 64 == 0
+  int M, N, K;        // per group; K % 8 == 0 (partial 64-wide k-blocks are zero-filled)
   int splits;         // split-K factor == cluster size along z
+  int stages;         // pipeline depth (host-chosen, <= 8)
+  int region;         // bytes of the pipeline / receive region before the barriers
   int epi, act;
   void* out;          // f16 (EPI_F16) or f32 base
   long long ldo;      // out row stride (elements)

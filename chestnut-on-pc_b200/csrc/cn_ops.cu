@@ -182,8 +182,8 @@ __global__ void __launch_bounds__(256) k_layernorm(const float* __restrict__ x, 
 }
 
 // -------------------------------------------------------------- attention
-// block per (clip, head); 8 warps; smem: Kt[hd][TP] f32, V[T][hd] f32,
-// q[8][hd] f32, P[8][TP] f32.
+// grid (clip*heads, ceil(T/8)); 8 warps, one query row each; smem: Kt[hd][TP]
+// f32, V[T][hd] f32, q[8][hd] f32, P[8][TP] f32.
 constexpr int kTP = 96;
 template <int HD>
 __global__ void __launch_bounds__(256) k_attention(const __half* __restrict__ qkv, __half* __restrict__ out, int T,
@@ -213,7 +213,9 @@ __global__ void __launch_bounds__(256) k_attention(const __half* __restrict__ qk
   const float scale = 1.0f / sqrtf((float)HD);
   float* q = Q + warp * HD;
   float* p = P + warp * kTP;
-  for (int t = warp; t < T; t += 8) {
+  {
+    const int t = blockIdx.y * 8 + warp;
+    if (t >= T) return;
     for (int i = lane; i < HD; i += 32) q[i] = __half2float(base[(size_t)t * ld + i]);
     __syncwarp();
     float s[3] = {0.f, 0.f, 0.f};
@@ -255,12 +257,14 @@ __global__ void __launch_bounds__(256) k_attention(const __half* __restrict__ qk
 }
 
 // ------------------------------------------------------------------ pool
-__global__ void __launch_bounds__(256) k_pool(const float* __restrict__ x, __half* __restrict__ pooled, int T, int d) {
+// grid (B, d/128), 128 threads: every CTA recomputes the 88 row statistics
+// (cheap, L2-resident) and owns 128 columns of the pooled feature.
+__global__ void __launch_bounds__(128) k_pool(const float* __restrict__ x, __half* __restrict__ pooled, int T, int d) {
   __shared__ float stat[2 * kTP];
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* xb = x + (size_t)b * T * d;
-  for (int t = warp; t < T; t += 8) {
+  for (int t = warp; t < T; t += 4) {
     const float* xr = xb + (size_t)t * d;
     float s = 0.f;
     for (int i = lane * 4; i < d; i += 128) {
@@ -284,12 +288,11 @@ __global__ void __launch_bounds__(256) k_pool(const float* __restrict__ x, __hal
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    float s = 0.f;
-    for (int t = 0; t < T; ++t)
-      s += __half2float(__float2half_rn((xb[(size_t)t * d + i] - stat[2 * t]) * stat[2 * t + 1]));
-    pooled[(size_t)b * d + i] = __float2half_rn(s / (float)T);
-  }
+  const int i = blockIdx.y * 128 + threadIdx.x;
+  float s = 0.f;
+  for (int t = 0; t < T; ++t)
+    s += __half2float(__float2half_rn((xb[(size_t)t * d + i] - stat[2 * t]) * stat[2 * t + 1]));
+  pooled[(size_t)b * d + i] = __float2half_rn(s / (float)T);
 }
 
 }  // namespace
@@ -347,20 +350,20 @@ int launch_attention(const __half* qkv, __half* out, int B, int T, int d, int he
       cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       set64 |= 1ull << dev;
     }
-    k_attention<64><<<B * heads, 256, smem, s>>>(qkv, out, T, d, heads);
+    k_attention<64><<<dim3(B * heads, (T + 7) / 8), 256, smem, s>>>(qkv, out, T, d, heads);
   } else {
     if (!(set128 & (1ull << dev))) {
       cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       set128 |= 1ull << dev;
     }
-    k_attention<128><<<B * heads, 256, smem, s>>>(qkv, out, T, d, heads);
+    k_attention<128><<<dim3(B * heads, (T + 7) / 8), 256, smem, s>>>(qkv, out, T, d, heads);
   }
   return (int)cudaGetLastError();
 }
 
 int launch_pool(const float* x, __half* pooled, int B, int T, int d, cudaStream_t s) {
   if (T > kTP || d % 128) return -2;
-  k_pool<<<B, 256, 0, s>>>(x, pooled, T, d);
+  k_pool<<<dim3(B, d / 128), 128, 0, s>>>(x, pooled, T, d);
   return (int)cudaGetLastError();
 }
 

@@ -113,8 +113,10 @@ int cn_param_info(int model, int index, char* name, int name_len, int* tensor_id
 
 /* ---- kernel-level entry points (device pointers, caller's stream) ------ */
 /* C[M][N] += A[M][K] * B, f16 inputs, f32 accumulate (WMMA D = C + A*B).
- * b_kmajor: 1 -> B is [N][K]; 0 -> B is [K][N].  K % 64 == 0.
- * bn / splits <= 0 choose a tiling automatically. */
+ * b_kmajor: 1 -> B is [N][K]; 0 -> B is [K][N].  K % 8 == 0, 16-byte aligned
+ * operands.  bn / splits <= 0 choose a tiling automatically.  The tensor-map
+ * plan of the last 16 distinct argument sets is cached, so repeated calls on
+ * the same buffers cost one launch. */
 int cn_gemm_wmma_f16(const void* A, const void* B, float* C, int M, int N, int K, int b_kmajor, int bn,
                      int splits, void* stream);
 /* out[r] = sum_i x[r][i] * w[i]; x f16 [rows][len], w f16 [len]; f32 out.

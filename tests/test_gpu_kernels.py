@@ -54,6 +54,9 @@ def test_gemm_config1_full_shape(b_kmajor, bn, splits):
     (130, 72, 192, 0, 64, 3),        # MN-major B with partial tiles
     (704, 1536, 512, 1, 0, 0),       # batch-8 clip shape (39M qkv)
     (64, 2811, 1024, 1, 0, 0),       # odd N (heads output width)
+    (1000, 32, 32, 1, 0, 0),         # K=32: half a k-block, zero-filled by TMA (39M stem 1x1 conv)
+    (300, 64, 288, 1, 64, 3),        # K=288 = 4.5 k-blocks (39M stem 3x3 conv)
+    (96, 40, 136, 0, 64, 2),         # MN-major B with a partial k-block
 ])
 def test_gemm_edge_shapes(M, N, K, b_kmajor, bn, splits):
     got, ref, mag, _ = _gemm(M, N, K, b_kmajor, bn, splits, seed=M + N)
