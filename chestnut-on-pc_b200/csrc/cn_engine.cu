@@ -170,8 +170,8 @@ static int gen_weights(cn_engine* e) {
     void* dst = e->wblob + e->poff[i];
     int r;
     if (p.kind == PK_W)
-      r = launch_fill_f16((__half*)dst, p.rows, p.cols, p.valid, seed, (uint64_t)p.tid, sqrtf(6.0f / (float)p.fan_in),
-                          e->stream);
+      r = launch_fill_f16_blocked((__half*)dst, p.rows, p.cols, p.valid, seed, (uint64_t)p.tid,
+                                  sqrtf(6.0f / (float)p.fan_in), e->stream);
     else if (p.kind == PK_B)
       r = launch_fill_f32((float*)dst, p.rows * p.cols, seed, (uint64_t)p.tid, 1.0f / sqrtf((float)p.fan_in),
                           e->stream);
@@ -193,7 +193,9 @@ static int layout_weights(cn_engine* e) {
   e->poff.assign(e->params.size(), 0);
   size_t off = 0;
   std::vector<bool> placed(e->params.size(), false);
-  auto bytes_of = [](const ParamDesc& p) { return (size_t)p.rows * p.cols * (p.kind == PK_W ? 2 : 4); };
+  auto bytes_of = [](const ParamDesc& p) {
+    return p.kind == PK_W ? (size_t)((p.cols + 63) / 64) * 64 * p.rows * 2 : (size_t)p.rows * p.cols * 4;
+  };
   for (size_t i = 0; i < e->params.size(); ++i) {
     if (placed[i]) continue;
     const std::string& n = e->params[i].name;
@@ -286,8 +288,9 @@ static cn_kernel_info kinfo(const char* name, dim3 g, dim3 b, dim3 cl, size_t sm
 static int add_gemm(cn_engine* e, const std::string& name, const void* A, long long lda, long long a_gs,
                     const void* Bw, long long ldb, long long b_gs, int M, int N, int K, int G, const GemmParams& ep) {
   GemmPlan g;
-  int r = gemm_plan(&g, A, lda, a_gs, Bw, ldb, b_gs, M, N, K, G, false, 0, 0, ep);
+  int r = gemm_plan(&g, A, lda, a_gs, Bw, ldb, b_gs, M, N, K, G, B_K_BLOCKED, 0, 0, ep);
   if (r) return r < 0 ? r : CN_ERR_CUDA;
+  g.pdl = true;
   const size_t idx = e->plans.size();
   e->plans.push_back(g);
   char nm[64];
@@ -321,11 +324,11 @@ static int build_plan(cn_engine* e) {
   {
     const long long vecs = 2LL * kFrameBytes / 16;
     e->steps.push_back({"push", [e, carry](cudaStream_t s) {
-                          return launch_push(e->d_warped, e->d_packed, carry, kNOut, e->rings, e->B, s);
+                          return launch_push(e->d_warped, e->d_packed, carry, kNOut, e->rings, e->B, s, true);
                         },
                         kinfo("queue_push", dim3((unsigned)((vecs + 255) / 256), B), dim3(256), dim3(1, 1, 1), 0)});
     e->steps.push_back({"gather0", [e](cudaStream_t s) {
-                          return launch_gather0(e->rings, e->d_packed, e->B, e->a0, e->cond16, e->feat16, s);
+                          return launch_gather0(e->rings, e->d_packed, e->B, e->a0, e->cond16, e->feat16, s, true);
                         },
                         kinfo("border_gather0", dim3(64, 2 * B + 1), dim3(128), dim3(1, 1, 1), 0)});
   }
@@ -349,7 +352,7 @@ static int build_plan(cn_engine* e) {
       char nm[64];
       snprintf(nm, sizeof(nm), "border_gather_s2:s%d", s);
       e->steps.push_back({nm, [src, dst, B, Hin, Win, Ci](cudaStream_t st) {
-                            return launch_gather_s2(src, 2, B, Hin, Win, Ci, dst, st);
+                            return launch_gather_s2(src, 2, B, Hin, Win, Ci, dst, st, true);
                           },
                           kinfo(nm, dim3((unsigned)std::min<long long>((total + 255) / 256, 1LL << 20)), dim3(256),
                                 dim3(1, 1, 1), 0)});
@@ -420,7 +423,7 @@ static int build_plan(cn_engine* e) {
       float* x = e->x;
       __half* h = e->h;
       const int d = m.d;
-      e->steps.push_back({"ln1", [x, h, R, d, bump](cudaStream_t s) { return launch_layernorm(x, h, R, d, bump, s); },
+      e->steps.push_back({"ln1", [x, h, R, d, bump](cudaStream_t s) { return launch_layernorm(x, h, R, d, bump, s, true); },
                           kinfo(("layernorm:" + pre + ".ln1").c_str(), dim3((R + 7) / 8), dim3(256), dim3(1, 1, 1), 0)});
     }
     CN_TRY(add_gemm(e, pre + ".qkv", e->h, m.d, 0, wptr(e, pre + ".qkv.w"), m.d, 0, R, 3 * m.d, m.d, 1,
@@ -430,8 +433,8 @@ static int build_plan(cn_engine* e) {
       __half* o = e->att;
       const int d = m.d, H = m.heads;
       const int hd = d / H;
-      const size_t smem = (size_t)(hd * 96 * 2 + 8 * hd + 8 * 96) * 4;
-      e->steps.push_back({"attn", [q, o, B, d, H](cudaStream_t s) { return launch_attention(q, o, B, kT, d, H, s); },
+      const size_t smem = attention_smem_bytes(hd);
+      e->steps.push_back({"attn", [q, o, B, d, H](cudaStream_t s) { return launch_attention(q, o, B, kT, d, H, s, true); },
                           kinfo(("attention:" + pre).c_str(), dim3(B * H, (kT + 7) / 8), dim3(256), dim3(1, 1, 1), smem)});
     }
     {
@@ -447,7 +450,7 @@ static int build_plan(cn_engine* e) {
       float* x = e->x;
       __half* h = e->h;
       const int d = m.d;
-      e->steps.push_back({"ln2", [x, h, R, d](cudaStream_t s) { return launch_layernorm(x, h, R, d, nullptr, s); },
+      e->steps.push_back({"ln2", [x, h, R, d](cudaStream_t s) { return launch_layernorm(x, h, R, d, nullptr, s, true); },
                           kinfo(("layernorm:" + pre + ".ln2").c_str(), dim3((R + 7) / 8), dim3(256), dim3(1, 1, 1), 0)});
     }
     CN_TRY(add_gemm(e, pre + ".fc1", e->h, m.d, 0, wptr(e, pre + ".fc1.w"), m.d, 0, R, m.mlp, m.d, 1,
@@ -463,11 +466,15 @@ static int build_plan(cn_engine* e) {
     }
   }
   {
-    const float* x = e->x;
+    // final LayerNorm (into h) then the token mean of each clip
+    float* x = e->x;
+    __half* h = e->h;
     __half* p = e->pooled;
     const int d = m.d;
-    e->steps.push_back({"pool", [x, p, B, d](cudaStream_t s) { return launch_pool(x, p, B, kT, d, s); },
-                        kinfo("ln_mean_pool", dim3(B, d / 128), dim3(128), dim3(1, 1, 1), 0)});
+    e->steps.push_back({"lnf", [x, h, R, d](cudaStream_t s) { return launch_layernorm(x, h, R, d, nullptr, s, true); },
+                        kinfo("layernorm:final", dim3((R + 7) / 8), dim3(256), dim3(1, 1, 1), 0)});
+    e->steps.push_back({"pool", [h, p, B, d](cudaStream_t s) { return launch_colmean(h, p, B, kT, d, s, true); },
+                        kinfo("token_mean_pool", dim3(B, d / 256), dim3(256), dim3(1, 1, 1), 0)});
   }
   {
     GemmParams ep = epi_f16(e->hid16, kFeat, 0, (const float*)wptr(e, "hid.b"), 0, ACT_TANH);
@@ -893,7 +900,7 @@ int cn_gemm_wmma_f16(const void* A, const void* B, float* C, int M, int N, int K
     ep.out = C;
     ep.ldo = N;
     const bool mn = !b_kmajor;
-    int r = gemm_plan(&g, A, K, 0, B, mn ? N : K, 0, M, N, K, 1, mn, bn, splits, ep);
+    int r = gemm_plan(&g, A, K, 0, B, mn ? N : K, 0, M, N, K, 1, mn ? B_MN_MAJOR : B_K_MAJOR, bn, splits, ep);
     if (r) return r < 0 ? r : CN_ERR_CUDA;
     std::lock_guard<std::mutex> lk(mu);
     keys[next] = key;

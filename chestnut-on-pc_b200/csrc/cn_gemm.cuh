@@ -13,12 +13,17 @@ enum Epi : int {
   EPI_F32_OUT = 4,    // out32[m][n] = acc + bias[n]
 };
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2, ACT_TANH = 3 };
+// Layouts of the B operand: row-major [N][K] (K contiguous), [K][N], or the
+// engine's k-blocked weight layout [KB][N][64] (one 64-wide k-block of every
+// row stored contiguously, so a weight tile is a single contiguous HBM run).
+enum BMode : int { B_K_MAJOR = 0, B_MN_MAJOR = 1, B_K_BLOCKED = 2 };
 
 struct GemmParams {
   int M, N, K;        // per group; K % 8 == 0 (partial 64-wide k-blocks are zero-filled)
   int splits;         // split-K factor == cluster size along z
   int stages;         // pipeline depth (host-chosen, <= 8)
   int region;         // bytes of the pipeline / receive region before the barriers
+  int prefetch;       // 1: residual / C rows are bulk-copied into shared memory
   int epi, act;
   void* out;          // f16 (EPI_F16) or f32 base
   long long ldo;      // out row stride (elements)
@@ -37,20 +42,22 @@ struct GemmParams {
 };
 
 struct GemmPlan {
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tx;  // A, B, and (prefetch only) the f32 output rows
   GemmParams p;
   dim3 grid;
   int bn;
-  bool b_mn;
+  int b_mode;
+  bool pdl;  // launch with programmatic stream serialization (frame graph only)
   size_t smem;
 };
 
 // A: [G][M][K] f16, row stride lda (elements), group stride a_gs (elements).
-// B: K-major [G][N][K] (row stride ldb) or, with b_mn, MN-major [G][K][N].
+// B: per b_mode, K-major [G][N][K] (row stride ldb), MN-major [G][K][N]
+// (row stride ldb), or k-blocked [G][ceil(K/64)][N][64] (ldb unused).
 // bn/splits <= 0 pick a tiling automatically.  Returns 0 or a cudaError_t /
 // CUresult code (also recorded in the engine's last-error string).
 int gemm_plan(GemmPlan* g, const void* A, long long lda, long long a_gs, const void* B, long long ldb,
-              long long b_gs, int M, int N, int K, int G, bool b_mn, int bn, int splits, const GemmParams& epi);
+              long long b_gs, int M, int N, int K, int G, int b_mode, int bn, int splits, const GemmParams& epi);
 int gemm_launch(const GemmPlan& g, cudaStream_t stream);
 int gemm_choose(int M, int N, int K, int G, int* bn, int* splits);
 

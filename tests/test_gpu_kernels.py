@@ -41,7 +41,7 @@ def _check(got, ref, mag):
 
 
 @pytest.mark.parametrize("b_kmajor", [1, 0])
-@pytest.mark.parametrize("bn,splits", [(0, 0), (64, 6), (128, 8), (256, 8), (128, 1), (256, 3)])
+@pytest.mark.parametrize("bn,splits", [(0, 0), (64, 6), (128, 8), (256, 1), (256, 8), (256, 3), (128, 1), (64, 3), (128, 5)])
 def test_gemm_config1_full_shape(b_kmajor, bn, splits):
     got, ref, mag, _ = _gemm(768, 256, 6144, b_kmajor, bn, splits)
     _check(got, ref, mag)
@@ -61,6 +61,18 @@ def test_gemm_config1_full_shape(b_kmajor, bn, splits):
 def test_gemm_edge_shapes(M, N, K, b_kmajor, bn, splits):
     got, ref, mag, _ = _gemm(M, N, K, b_kmajor, bn, splits, seed=M + N)
     _check(got, ref, mag)
+
+
+def test_gemm_rejects_unsupported_tilings():
+    from chestnut_b200 import ChestnutError
+    dA, dB, dC = DeviceBuffer(768 * 6144 * 2), DeviceBuffer(256 * 6144 * 2), DeviceBuffer(768 * 256 * 4)
+    with pytest.raises(ChestnutError, match="unsupported tiling"):
+        kernels.gemm_wmma_f16(dA.ptr, dB.ptr, dC.ptr, 768, 256, 6144, 1, 96, 2)      # bn not 64/128/256
+    with pytest.raises(ChestnutError, match="unsupported tiling"):
+        kernels.gemm_wmma_f16(dA.ptr, dB.ptr, dC.ptr, 768, 256, 64, 1, 128, 2)       # more splits than k-blocks
+    with pytest.raises(ChestnutError, match="unsupported tiling"):
+        kernels.gemm_wmma_f16(dA.ptr, dB.ptr, dC.ptr, 768, 256, 6144, 1, 128, 9)     # cluster larger than 8
+    assert kernels.device_error() == 0
 
 
 def test_gemm_accumulates_onto_c():
