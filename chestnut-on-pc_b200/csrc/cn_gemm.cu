@@ -39,6 +39,7 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kA_Bytes = 128 * 64 * 2;
 constexpr size_t kMaxDynSmem = 227 * 1024;
+constexpr int kMaxSplits = 16;  // split-K cluster size (above 8 uses non-portable clusters)
 
 template <int BN>
 struct Tile {
@@ -428,6 +429,9 @@ int launch_plan(const GemmPlan& g, cudaStream_t stream) {
     if (!attr_set.count(key)) {
       cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDynSmem);
+      if (e == cudaSuccess)  // split-K clusters of up to 16 CTAs
+        e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                                 cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (e != cudaSuccess) {
         set_last_error("cudaFuncSetAttribute(smem=%zu): %s", kMaxDynSmem, cudaGetErrorString(e));
         return (int)e;
@@ -499,6 +503,7 @@ static int max_active_clusters(int bn, int K, int splits) {
   KernelFn kern = pick_kernel(bn, B_K_BLOCKED, EPI_F16);
   cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)kMaxDynSmem);
+  cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, 1, splits);
   cfg.blockDim = dim3(kThreads);
@@ -535,7 +540,7 @@ int gemm_choose(int M, int N, int K, int G, int* bn_out, int* s_out) {
     const int nt = (N + bn - 1) / bn;
     if (bn > 64 && N <= bn / 2) continue;
     const int nch = bn / (bn < 128 ? bn : 128);
-    for (int s = 1; s <= 8 && s <= KB; ++s) {
+    for (int s = 1; s <= kMaxSplits && s <= KB; ++s) {
       int st_, reg_;
       size_t smem_;
       gemm_smem_layout(bn, K, s, false, &st_, &reg_, &smem_);
@@ -575,7 +580,7 @@ int gemm_plan(GemmPlan* g, const void* A, long long lda, long long a_gs, const v
     return -2;
   }
   if (bn <= 0 || splits <= 0) gemm_choose(M, N, K, G, &bn, &splits);
-  if (!(bn == 64 || bn == 128 || bn == 256) || splits < 1 || splits > 8 || splits > (K + 63) / 64) {
+  if (!(bn == 64 || bn == 128 || bn == 256) || splits < 1 || splits > kMaxSplits || splits > (K + 63) / 64) {
     set_last_error("gemm_plan: unsupported tiling bn=%d splits=%d", bn, splits);
     return -2;
   }

@@ -3,4 +3,5 @@
 #include "cn_gemm.cu"
 #include "cn_reduce.cu"
 #include "cn_ops.cu"
+#include "cn_attn.cu"
 #include "cn_engine.cu"

@@ -75,39 +75,49 @@ __device__ __forceinline__ __half norm_u8(uint32_t u) {
   return __float2half_rn(__fmul_rn(__int2float_rn((int)u - 128), 0.015625f));
 }
 
-// grid (64, 2B + 1), block 128.  y < 2B: camera (b, cam) first-conv gather;
+// grid (64, 2B + 1), block 128.  y < 2B: camera (b, cam), output row oy =
+// blockIdx.x: the three input rows 2oy-1..2oy+1 of the 12 sampled planes are
+// staged in shared memory (coalesced), then thread ox builds its 128-wide
+// im2col row.  Out-of-range texels read as 0 after normalisation (the image2d
+// border rule); the address itself is clamped, so no read leaves the frame.
 // y == 2B: cond vector + features_buffer for clip blockIdx.x.
 __global__ void __launch_bounds__(128) k_gather0(Rings r, const float* __restrict__ packed, int B,
                                                  __half* __restrict__ a0, __half* __restrict__ cond16,
                                                  __half* __restrict__ feat16) {
   pdl_trigger();
   pdl_wait();
+  __shared__ __align__(16) uint8_t rows_s[12][3][kW];
   const int c = *r.ctr;  // frames pushed before this one; this frame sits in slot c % 5
   if (blockIdx.y < 2 * B) {
     const int b = blockIdx.y >> 1, cam = blockIdx.y & 1;
-    const int pos = blockIdx.x * 128 + threadIdx.x;  // 0..8191
-    const int oy = pos >> 7, ox = pos & 127;
+    const int oy = blockIdx.x, ox = threadIdx.x;
     const uint8_t* base = r.img + ((size_t)b * 2 + cam) * kImgQ * kFrameBytes;
     // sample_skip over the 5-row queue after the push: rows 0 (oldest) and 4 (newest)
     const uint8_t* f_old = base + (size_t)((c + 1) % kImgQ) * kFrameBytes;
     const uint8_t* f_new = base + (size_t)(c % kImgQ) * kFrameBytes;
+    for (int i = threadIdx.x; i < 12 * 3 * (kW / 16); i += 128) {
+      const int ch = i / (3 * (kW / 16)), rr = (i / (kW / 16)) % 3, q = i % (kW / 16);
+      const int y = min(max(2 * oy + rr - 1, 0), kH - 1);
+      const uint8_t* plane = ch < 6 ? f_old + (size_t)ch * kH * kW : f_new + (size_t)(ch - 6) * kH * kW;
+      *reinterpret_cast<uint4*>(&rows_s[ch][rr][q * 16]) = *reinterpret_cast<const uint4*>(plane + y * kW + q * 16);
+    }
+    __syncthreads();
     __align__(16) __half row[kK0Pad];
 #pragma unroll
     for (int tap = 0; tap < 9; ++tap) {
-      const int y = 2 * oy + tap / 3 - 1, x = 2 * ox + tap % 3 - 1;
+      const int ky = tap / 3, kx = tap % 3;
+      const int y = 2 * oy + ky - 1, x = 2 * ox + kx - 1;
       const bool valid = (unsigned)y < (unsigned)kH && (unsigned)x < (unsigned)kW;
-      const int yc = min(max(y, 0), kH - 1), xc = min(max(x, 0), kW - 1);  // address stays in bounds
-      const int off = yc * kW + xc;
+      const int xc = min(max(x, 0), kW - 1);
 #pragma unroll
       for (int ch = 0; ch < 12; ++ch) {
-        const uint8_t* plane = (ch < 6 ? f_old + (size_t)ch * kH * kW : f_new + (size_t)(ch - 6) * kH * kW);
-        const __half v = norm_u8(plane[off]);
+        const __half v = norm_u8(rows_s[ch][ky][xc]);
         row[tap * 12 + ch] = valid ? v : __float2half_rn(0.0f);
       }
     }
 #pragma unroll
     for (int k = kK0; k < kK0Pad; ++k) row[k] = __float2half_rn(0.0f);
-    uint4* dst = reinterpret_cast<uint4*>(a0 + ((size_t)cam * B * 8192 + (size_t)b * 8192 + pos) * kK0Pad);
+    uint4* dst = reinterpret_cast<uint4*>(a0 + ((size_t)cam * B * 8192 + (size_t)b * 8192 + oy * 128 + ox) * kK0Pad);
     const uint4* src = reinterpret_cast<const uint4*>(row);
 #pragma unroll
     for (int q = 0; q < kK0Pad / 8; ++q) dst[q] = src[q];
@@ -163,37 +173,48 @@ __global__ void k_gather_s2(const __half* __restrict__ act, int G, int B, int Hi
 }
 
 // ------------------------------------------------------------ layer norm
-template <int NV>  // float4 per lane; d = NV * 128
+// 4 warps per row (each a quarter of the row), 2 rows per 256-thread block;
+// per-warp partial sums are combined in warp order, so the result is
+// deterministic.  NV = float4 per lane, d = NV * 512.
+template <int NV>
 __global__ void __launch_bounds__(256) k_layernorm(const float* __restrict__ x, __half* __restrict__ y, int rows,
                                                    int* bump) {
   pdl_trigger();
   pdl_wait();
+  __shared__ float part[2][4][2];
+  constexpr int d = NV * 512;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + warp;
+  const int slot = warp >> 2, q = warp & 3;
+  const int row = blockIdx.x * 2 + slot;
   if (bump && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(bump, 1);
-  if (row >= rows) return;
-  constexpr int d = NV * 128;
-  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * d);
+  const bool live = row < rows;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(live ? row : 0) * d + q * (d / 4));
   float4 v[NV];
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    v[i] = xr[lane + 32 * i];
+    v[i] = live ? xr[lane + 32 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
     s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const float mean = s / (float)d;
-  float q = 0.f;
+  if (lane == 0) part[slot][q][0] = s;
+  __syncthreads();
+  const float mean = (((part[slot][0][0] + part[slot][1][0]) + part[slot][2][0]) + part[slot][3][0]) / (float)d;
+  float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
-    q += (a * a + b * b) + (c * c + e * e);
+    ss += (a * a + b * b) + (c * c + e * e);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-  const float rstd = 1.0f / sqrtf(q / (float)d + 1e-5f);
-  uint2* yr = reinterpret_cast<uint2*>(y + (size_t)row * d);
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) part[slot][q][1] = ss;
+  __syncthreads();
+  const float var = (((part[slot][0][1] + part[slot][1][1]) + part[slot][2][1]) + part[slot][3][1]) / (float)d;
+  const float rstd = 1.0f / sqrtf(var + 1e-5f);
+  if (!live) return;
+  uint2* yr = reinterpret_cast<uint2*>(y + (size_t)row * d + q * (d / 4));
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     __half2 h0 = __floats2half2_rn((v[i].x - mean) * rstd, (v[i].y - mean) * rstd);
@@ -205,102 +226,7 @@ __global__ void __launch_bounds__(256) k_layernorm(const float* __restrict__ x, 
   }
 }
 
-// -------------------------------------------------------------- attention
-// grid (clip*heads, ceil(T/8)); 8 warps, one query row each.
-// smem: Kt[HD][kTP] f32 (keys transposed, lane j reads key j), V[kTP][HD+1]
-// f32 (odd stride: conflict-free), q[8][HD] f32, P[8][kTP] f32.
-constexpr int kTP = 96;
-template <int HD>
-__global__ void __launch_bounds__(256) k_attention(const __half* __restrict__ qkv, __half* __restrict__ out, int T,
-                                                   int d, int heads) {
-  extern __shared__ float sm[];
-  pdl_trigger();
-  pdl_wait();
-  constexpr int VL = HD + 1;
-  float* Kt = sm;
-  float* V = Kt + HD * kTP;
-  float* Q = V + kTP * VL;
-  float* P = Q + 8 * HD;
-  const int b = blockIdx.x / heads, h = blockIdx.x % heads;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t ld = 3 * (size_t)d;
-  const __half* base = qkv + (size_t)b * T * ld + (size_t)h * HD;
-  // stage K and V: consecutive threads take consecutive tokens of one 8-wide
-  // column chunk, all loads of a thread issued before any store
-  constexpr int NCH = kTP * (HD / 8);
-  constexpr int PER = (NCH + 255) / 256;
-  uint4 kv[PER], vv[PER];
-#pragma unroll
-  for (int it = 0; it < PER; ++it) {
-    const int idx = threadIdx.x + it * 256;
-    const int t = idx % kTP, c8 = (idx / kTP) * 8;
-    kv[it] = make_uint4(0, 0, 0, 0);
-    vv[it] = make_uint4(0, 0, 0, 0);
-    if (idx < NCH && t < T) {
-      kv[it] = *reinterpret_cast<const uint4*>(base + (size_t)t * ld + d + c8);
-      vv[it] = *reinterpret_cast<const uint4*>(base + (size_t)t * ld + 2 * d + c8);
-    }
-  }
-#pragma unroll
-  for (int it = 0; it < PER; ++it) {
-    const int idx = threadIdx.x + it * 256;
-    if (idx >= NCH) continue;
-    const int t = idx % kTP, c8 = (idx / kTP) * 8;
-    const __half* kh = reinterpret_cast<const __half*>(&kv[it]);
-    const __half* vh = reinterpret_cast<const __half*>(&vv[it]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      Kt[(c8 + j) * kTP + t] = __half2float(kh[j]);
-      V[t * VL + c8 + j] = __half2float(vh[j]);
-    }
-  }
-  __syncthreads();
-  const int t = blockIdx.y * 8 + warp;
-  if (t >= T) return;
-  const float scale = 1.0f / sqrtf((float)HD);
-  float* q = Q + warp * HD;
-  float* p = P + warp * kTP;
-  for (int i = lane; i < HD; i += 32) q[i] = __half2float(base[(size_t)t * ld + i]);
-  __syncwarp();
-  float s[3] = {0.f, 0.f, 0.f};
-#pragma unroll 8
-  for (int i = 0; i < HD; ++i) {
-    const float qi = q[i];
-#pragma unroll
-    for (int u = 0; u < 3; ++u) s[u] = fmaf(qi, Kt[i * kTP + lane + 32 * u], s[u]);
-  }
-  float mx = -INFINITY;
-#pragma unroll
-  for (int u = 0; u < 3; ++u) {
-    s[u] = (lane + 32 * u < T) ? s[u] * scale : -INFINITY;
-    mx = fmaxf(mx, s[u]);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float e[3], sum = 0.f;
-#pragma unroll
-  for (int u = 0; u < 3; ++u) {
-    e[u] = (lane + 32 * u < T) ? expf(s[u] - mx) : 0.f;
-    sum += e[u];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-#pragma unroll
-  for (int u = 0; u < 3; ++u) p[lane + 32 * u] = e[u] / sum;
-  __syncwarp();
-  float acc[HD / 32];
-#pragma unroll
-  for (int i = 0; i < HD / 32; ++i) acc[i] = 0.f;
-#pragma unroll 4
-  for (int j = 0; j < T; ++j) {
-    const float pj = p[j];
-#pragma unroll
-    for (int i = 0; i < HD / 32; ++i) acc[i] = fmaf(pj, V[j * VL + lane + 32 * i], acc[i]);
-  }
-  __half* o = out + ((size_t)b * T + t) * d + (size_t)h * HD;
-#pragma unroll
-  for (int i = 0; i < HD / 32; ++i) o[lane + 32 * i] = __float2half_rn(acc[i]);
-}
+constexpr int kTP = 96;  // max tokens per clip handled by the pooling kernels
 
 // ------------------------------------------------------------------ pool
 // Mean over the T tokens of each clip of the (already f16-rounded) final
@@ -359,38 +285,14 @@ int launch_gather_s2(const __half* act, int G, int B, int Hin, int Win, int C, _
 }
 
 int launch_layernorm(const float* x, __half* y, int rows, int d, int* bump, cudaStream_t s, bool pdl) {
-  const dim3 g((unsigned)((rows + 7) / 8));
+  const dim3 g((unsigned)((rows + 1) / 2));
   switch (d) {
-    case 512: return (int)launch_ex(k_layernorm<4>, g, dim3(256), 0, s, pdl, x, y, rows, bump);
-    case 1024: return (int)launch_ex(k_layernorm<8>, g, dim3(256), 0, s, pdl, x, y, rows, bump);
-    case 2048: return (int)launch_ex(k_layernorm<16>, g, dim3(256), 0, s, pdl, x, y, rows, bump);
+    case 512: return (int)launch_ex(k_layernorm<1>, g, dim3(256), 0, s, pdl, x, y, rows, bump);
+    case 1024: return (int)launch_ex(k_layernorm<2>, g, dim3(256), 0, s, pdl, x, y, rows, bump);
+    case 2048: return (int)launch_ex(k_layernorm<4>, g, dim3(256), 0, s, pdl, x, y, rows, bump);
     default: return -2;
   }
 }
-
-int launch_attention(const __half* qkv, __half* out, int B, int T, int d, int heads, cudaStream_t s, bool pdl) {
-  const int hd = d / heads;
-  if (T > kTP || (hd != 64 && hd != 128)) return -2;
-  const size_t smem = attention_smem_bytes(hd);
-  static unsigned long long set64 = 0, set128 = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (hd == 64) {
-    if (!(set64 & (1ull << dev))) {
-      cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      set64 |= 1ull << dev;
-    }
-    return (int)launch_ex(k_attention<64>, dim3(B * heads, (T + 7) / 8), dim3(256), smem, s, pdl, qkv, out, T, d, heads);
-  }
-  if (!(set128 & (1ull << dev))) {
-    cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    set128 |= 1ull << dev;
-  }
-  return (int)launch_ex(k_attention<128>, dim3(B * heads, (T + 7) / 8), dim3(256), smem, s, pdl, qkv, out, T, d,
-                        heads);
-}
-
-size_t attention_smem_bytes(int hd) { return (size_t)(hd * kTP + kTP * (hd + 1) + 8 * hd + 8 * kTP) * sizeof(float); }
 
 int launch_colmean(const __half* y, __half* pooled, int B, int T, int d, cudaStream_t s, bool pdl) {
   if (d % 256) return -2;

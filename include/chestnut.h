@@ -114,7 +114,8 @@ int cn_param_info(int model, int index, char* name, int name_len, int* tensor_id
 /* ---- kernel-level entry points (device pointers, caller's stream) ------ */
 /* C[M][N] += A[M][K] * B, f16 inputs, f32 accumulate (WMMA D = C + A*B).
  * b_kmajor: 1 -> B is [N][K]; 0 -> B is [K][N].  K % 8 == 0, 16-byte aligned
- * operands.  bn / splits <= 0 choose a tiling automatically.  The tensor-map
+ * operands; bn in {64,128,256}, splits in [1,16] (<= K/64); bn / splits <= 0
+ * choose a tiling automatically.  The tensor-map
  * plan of the last 16 distinct argument sets is cached, so repeated calls on
  * the same buffers cost one launch. */
 int cn_gemm_wmma_f16(const void* A, const void* B, float* C, int M, int N, int K, int b_kmajor, int bn,

@@ -41,7 +41,7 @@ def _check(got, ref, mag):
 
 
 @pytest.mark.parametrize("b_kmajor", [1, 0])
-@pytest.mark.parametrize("bn,splits", [(0, 0), (64, 6), (128, 8), (256, 1), (256, 8), (256, 3), (128, 1), (64, 3), (128, 5)])
+@pytest.mark.parametrize("bn,splits", [(0, 0), (64, 6), (128, 8), (256, 1), (256, 8), (256, 3), (256, 16), (128, 12), (128, 1), (64, 3), (128, 5)])
 def test_gemm_config1_full_shape(b_kmajor, bn, splits):
     got, ref, mag, _ = _gemm(768, 256, 6144, b_kmajor, bn, splits)
     _check(got, ref, mag)
@@ -71,7 +71,7 @@ def test_gemm_rejects_unsupported_tilings():
     with pytest.raises(ChestnutError, match="unsupported tiling"):
         kernels.gemm_wmma_f16(dA.ptr, dB.ptr, dC.ptr, 768, 256, 64, 1, 128, 2)       # more splits than k-blocks
     with pytest.raises(ChestnutError, match="unsupported tiling"):
-        kernels.gemm_wmma_f16(dA.ptr, dB.ptr, dC.ptr, 768, 256, 6144, 1, 128, 9)     # cluster larger than 8
+        kernels.gemm_wmma_f16(dA.ptr, dB.ptr, dC.ptr, 768, 256, 6144, 1, 128, 17)    # cluster larger than 16
     assert kernels.device_error() == 0
 
 
