@@ -112,6 +112,7 @@ def run_ours(args, rank, world, local_rank):
     eng = Engine(args.model, device=dev, batch=B, seed=args.seed, carry_hidden=True)
     stream = torch.cuda.ExternalStream(eng.stream_handle(), device=dev)
     n_launch = eng.info()["n_kernels"]
+    eng_info = eng.info()
     rng = np.random.default_rng(1000 + rank)
     nfr = 8
     w, pk = frame_inputs(rng, nfr, B)
@@ -175,8 +176,14 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = e0.elapsed_time(e1)
     digest = float(np.abs(out_np).sum())
 
+    eng.close()
+
+    # ---- config 5: clip throughput of the 39M model, 8 clips per launch
+    clip = clip_throughput(args, rank, world, dev, dist, barrier) if args.clips > 0 else None
+
     # ---- max over ranks, gather clip digests (the only collective)
-    vals = torch.tensor([total_ms, e2e_ms, digest], dtype=torch.float64, device=f"cuda:{dev}")
+    vals = torch.tensor([total_ms, e2e_ms, digest, clip["ms"] if clip else 0.0], dtype=torch.float64,
+                        device=f"cuda:{dev}")
     if dist:
         allv = [torch.zeros_like(vals) for _ in range(world)]
         dist.all_gather(allv, vals)
@@ -186,7 +193,6 @@ def run_ours(args, rank, world, local_rank):
     for p in (hw, hp, ho):
         lib().cn_host_free_pinned(p)
     if rank != 0:
-        eng.close()
         if dist:
             dist.barrier()
             dist.destroy_process_group()
@@ -195,12 +201,12 @@ def run_ours(args, rank, world, local_rank):
     max_e2e = float(allv[:, 1].max())
     frames = args.steps * B * world
     hbm, tf, src = peaks()
-    info = eng.info()
     d = 2048 if args.model == "1b" else 512
     mlp = 4 * d
     rows = 88 * B
     fc2_bytes = mlp * d * 2 + rows * mlp * 2 + rows * d * 4 * 2 + d * 4
     k_avg = statistics.mean(kms) if kms else float("nan")
+    info = eng_info
     achieved = fc2_bytes / (k_avg * 1e-3) / 1e9
     line = {
         "metric": METRIC,
@@ -237,13 +243,65 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk.summary(),
         "clip_digests": allv[:, 2].tolist(),
     }
+    if clip:
+        cms = float(allv[:, 3].max())
+        line["clip_throughput"] = {
+            "workload": f"config 5: {args.clips} synthetic 39M clips x {args.clip_frames} frames, {clip['batch']} clips "
+                        f"per graph launch, round-robin over {world} GPU(s), per-clip results all-gathered once at "
+                        "clip end", "value": args.clips * args.clip_frames / (cms * 1e-3), "unit": "frames/s",
+            "ms": cms, "scaling": "strong", "path": "public run_frame with host buffers (H2D + D2H per frame)",
+            "gathered_checksum": clip["checksum"]}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.model, budget_s=args.cpu_budget)
-    eng.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     return line
+
+
+def clip_throughput(args, rank, world, dev, dist, barrier):
+    """Config 5: this rank's share of the clips, 8 per launch, frames through run_frame."""
+    import torch
+    from chestnut_b200 import Engine, clips
+
+    B = 8
+    mine = clips.assign(args.clips, world, rank)
+    eng = Engine("39m", device=dev, batch=B, seed=args.seed)
+    stream = torch.cuda.ExternalStream(eng.stream_handle(), device=dev)
+    # clip c, frame f reads pool frame (c + f) % 4 with clip-specific desire: a pure
+    # function of (clip, frame), so the gathered results match for any GPU count
+    rng = np.random.default_rng(77)
+    pool = rng.integers(0, 256, (4, 2, 6, 128, 256), dtype=np.uint8)
+    staged = {}
+    for group in clips.batches(mine, B):
+        for f4 in range(4):
+            w = np.stack([pool[(c + f4) % 4] for c in group])
+            pk = np.zeros((len(group), 524), np.float32)
+            for i, c in enumerate(group):
+                pk[i, c % 8] = 1.0
+                pk[i, 8 + c % 2] = 1.0
+            staged[(tuple(group), f4)] = (w, pk)
+
+    def batch_source(group, f):
+        w, pk = staged[(tuple(group), f % 4)]
+        return w, pk.copy()
+
+    def factory(n):
+        return eng if n == B else Engine("39m", device=dev, batch=n, seed=args.seed)
+
+    clips.run_rank(factory, None, clips.batches(mine, B)[0], 3, B, batch_source)  # warm-up
+    eng.reset()
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    res = clips.run_rank(factory, None, mine, args.clip_frames, B, batch_source)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    sums, _ = clips.gather(res, args.clips, args.clip_frames, 3323, dist, device=f"cuda:{dev}")
+    eng.close()
+    return {"ms": ms, "batch": B, "checksum": float(np.abs(sums).sum())}
 
 
 def cpu_baseline(model, budget_s=25.0, max_frames=None):
@@ -294,6 +352,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-budget", type=float, default=25.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--clips", type=int, default=64, help="config-5 clips (0 skips the clip-throughput leg)")
+    ap.add_argument("--clip-frames", type=int, default=30, help="frames per clip in the clip-throughput leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -51,6 +51,7 @@ _SIGS = {
     "cn_state_bytes": ([], _sz),
     "cn_get_state": ([_vp, _i, _vp, _sz], _i),
     "cn_set_state": ([_vp, _i, _vp, _sz], _i),
+    "cn_reset_state": ([_vp], _i),
     "cn_kernel_list": ([_vp, ctypes.POINTER(cn_kernel_info), ctypes.POINTER(_i)], _i),
     "cn_profile_frame": ([_vp, _vp, _vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_i)], _i),
     "cn_set_timed_class": ([_vp, ctypes.c_char_p], _i),

@@ -110,6 +110,10 @@ class Engine:
         buf = np.concatenate(parts)
         check(lib().cn_set_state(self._h, clip, buf.ctypes.data, buf.nbytes), "cn_set_state")
 
+    def reset(self):
+        """Start new clips: zero the queues, carried hidden state and frame counter."""
+        check(lib().cn_reset_state(self._h), "cn_reset_state")
+
     # -- introspection -----------------------------------------------------
     def kernel_list(self):
         n = ctypes.c_int(0)

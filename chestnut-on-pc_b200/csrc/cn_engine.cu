@@ -755,6 +755,18 @@ int cn_set_state(cn_engine* e, int clip, const void* buf, size_t bytes) {
   return 0;
 }
 
+int cn_reset_state(cn_engine* e) {
+  if (!e) return CN_ERR_ARG;
+  CN_CUDA(cudaSetDevice(e->cfg.device));
+  CN_CUDA(cudaMemsetAsync(e->rings.img, 0, (size_t)e->B * 2 * kImgQ * kFrameBytes, e->stream));
+  CN_CUDA(cudaMemsetAsync(e->rings.feat, 0, (size_t)e->B * kFeatQ * kFeat * 4, e->stream));
+  CN_CUDA(cudaMemsetAsync(e->rings.desire, 0, (size_t)e->B * kDesireQ * kDesire * 4, e->stream));
+  CN_CUDA(cudaMemsetAsync(e->rings.ctr, 0, sizeof(int), e->stream));
+  CN_CUDA(cudaMemsetAsync(e->out, 0, (size_t)e->B * kNOut * 4, e->stream));
+  CN_CUDA(cudaStreamSynchronize(e->stream));
+  return 0;
+}
+
 int cn_kernel_list(cn_engine* e, cn_kernel_info* out, int* n_inout) {
   if (!e || !n_inout) return CN_ERR_ARG;
   const int n = (int)e->steps.size();

@@ -95,6 +95,8 @@ int cn_sync(cn_engine* e);
 size_t cn_state_bytes(void);
 int cn_get_state(cn_engine* e, int clip, void* buf, size_t bytes);
 int cn_set_state(cn_engine* e, int clip, const void* buf, size_t bytes);
+/* Zero every clip's queues, carried hidden state and frame counter (a new clip). */
+int cn_reset_state(cn_engine* e);
 int cn_kernel_list(cn_engine* e, cn_kernel_info* out, int* n_inout);
 /* Eager run of one frame with an event pair around every launch; ms[i] is
  * the duration of kernel i of cn_kernel_list. */

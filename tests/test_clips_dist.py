@@ -1,0 +1,94 @@
+"""CPU tests of the clip-sharding host logic, with world_size-2 gloo ranks.
+
+A fake engine stands in for the GPU: it is a deterministic function of the
+frame inputs and the carried hidden state, so a sharded run must reproduce the
+single-process run bit for bit.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from chestnut_b200 import clips
+
+N_OUT = 3323
+
+
+class FakeEngine:
+    def __init__(self, batch):
+        self.batch = batch
+
+    def run_frame(self, warped, packed):
+        w = warped.reshape(self.batch, -1).astype(np.float64)
+        h = packed[:, 12:].astype(np.float64)
+        base = w[:, ::4097][:, :N_OUT - 512].mean(axis=1, keepdims=True) / 255.0
+        head = np.tile(base, (1, N_OUT - 512)) + np.arange(N_OUT - 512) * 1e-4
+        hid = np.tanh(0.5 * h + base)
+        return np.concatenate([head, hid], axis=1).astype(np.float32)
+
+
+def frame_source(clip, frame):
+    rs = np.random.default_rng(1000 * clip + frame)
+    w = rs.integers(0, 256, (2, 6, 128, 256), dtype=np.uint8)
+    pk = np.zeros(524, np.float32)
+    pk[clip % 8] = 1.0
+    pk[8] = 1.0
+    return w, pk
+
+
+def test_assign_round_robin_covers_every_clip_once():
+    n, world = 64, 8
+    owned = [clips.assign(n, world, r) for r in range(world)]
+    flat = sorted(c for o in owned for c in o)
+    assert flat == list(range(n))
+    assert all(len(o) == n // world for o in owned)
+    assert clips.batches(owned[0], 8) == [owned[0]]
+    assert clips.batches(list(range(10)), 4) == [[0, 1, 2, 3], [4, 5, 6, 7], [8, 9]]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, n_clips, n_frames, batch, out_path):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    mine = clips.assign(n_clips, world, rank)
+    res = clips.run_rank(FakeEngine, frame_source, mine, n_frames, batch)
+    sums, finals = clips.gather(res, n_clips, n_frames, N_OUT, dist)
+    if rank == 0:
+        np.savez(out_path, sums=sums, finals=finals)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_run_equals_single_process(tmp_path):
+    n_clips, n_frames, batch, world = 6, 4, 2, 2
+    ref = clips.run_rank(FakeEngine, frame_source, list(range(n_clips)), n_frames, batch)
+    ref_s, ref_f = clips.gather(ref, n_clips, n_frames, N_OUT, None)
+    out_path = str(tmp_path / "gathered.npz")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, n_clips, n_frames, batch, out_path))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    z = np.load(out_path)
+    assert np.array_equal(z["sums"], ref_s)
+    assert np.array_equal(z["finals"], ref_f)
+
+
+def test_batching_does_not_change_results():
+    a = clips.run_rank(FakeEngine, frame_source, [0, 1, 2], 3, 1)
+    b = clips.run_rank(FakeEngine, frame_source, [0, 1, 2], 3, 3)
+    for c in (0, 1, 2):
+        assert np.array_equal(a[c][0], b[c][0]) and np.array_equal(a[c][1], b[c][1])
