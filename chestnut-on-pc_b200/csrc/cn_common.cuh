@@ -72,14 +72,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (and records `code`) if the phase did not flip
-// within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+// within limit_ns.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       set_dev_error(code);
       return false;
     }

@@ -930,7 +930,7 @@ int cn_reduce_rows_f16(const void* x, const void* w, float* out, long long rows,
     set_last_error("cn_reduce_rows_f16: need rows in [1, 65535], len %% 8 == 0 and 16-byte aligned x, w");
     return CN_ERR_ARG;
   }
-  if (cpr <= 0) cpr = rows >= 1184 ? 8 : 8;
+  if (cpr <= 0) cpr = rows >= 1184 ? 1 : (rows >= 296 ? 4 : 8);  // enough rows alone fill the GPU
   if (cpr != 1 && cpr != 2 && cpr != 4 && cpr != 8) {
     set_last_error("cn_reduce_rows_f16: chunks_per_row must be 1, 2, 4 or 8");
     return CN_ERR_ARG;
@@ -959,6 +959,18 @@ int cn_border_gather_s2(const void* act, int G, int B, int H, int W, int C, void
 int cn_device_error(int* code) {
   if (!code) return CN_ERR_ARG;
   int r = device_error_read_and_clear(0, code);
+  return r ? CN_ERR_CUDA : 0;
+}
+
+int cn_selftest_bounded_wait(int limit_ms, int* code) {
+  if (!code || limit_ms < 1 || limit_ms > 10000) return CN_ERR_ARG;
+  int r = launch_selftest_wait((unsigned long long)limit_ms * 1000000ull, 0);
+  if (r) {
+    set_last_error("selftest launch failed: %s", cudaGetErrorString((cudaError_t)r));
+    return CN_ERR_CUDA;
+  }
+  CN_CUDA(cudaDeviceSynchronize());
+  r = device_error_read_and_clear(0, code);
   return r ? CN_ERR_CUDA : 0;
 }
 

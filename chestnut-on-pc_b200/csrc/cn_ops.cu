@@ -245,7 +245,23 @@ __global__ void __launch_bounds__(256) k_colmean(const __half* __restrict__ y, _
   pooled[(size_t)b * d + i] = __float2half_rn(s / (float)T);
 }
 
+// Failure-detection self-test: wait on a barrier nothing arrives on.
+__global__ void k_selftest_wait(unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, 9, limit_ns);
+}
+
 }  // namespace
+
+int launch_selftest_wait(unsigned long long limit_ns, cudaStream_t s) {
+  k_selftest_wait<<<1, 32, 0, s>>>(limit_ns);
+  return (int)cudaGetLastError();
+}
 
 int launch_fill_f16(__half* dst, long long rows, long long cols, long long valid_cols, uint64_t seed, uint64_t tid,
                     float bound, cudaStream_t s) {

@@ -51,6 +51,8 @@ int launch_attention(const __half* qkv, __half* out, int B, int T, int d, int he
 int launch_colmean(const __half* y, __half* pooled, int B, int T, int d, cudaStream_t s, bool pdl = false);
 size_t attention_smem_bytes(int hd);
 
+int launch_selftest_wait(unsigned long long limit_ns, cudaStream_t s);
+
 int reduce_rows_launch(const void* x, const void* w, float* out, long long rows, long long len, int cpr,
                        cudaStream_t stream);
 

@@ -131,6 +131,10 @@ int cn_reduce_rows_f16(const void* x, const void* w, float* out, long long rows,
 int cn_border_gather_s2(const void* act, int G, int B, int H, int W, int C, void* out, void* stream);
 /* Read (and clear) the device error word. */
 int cn_device_error(int* code);
+/* Failure-detection self-test: launches one CTA that waits on an mbarrier no
+ * one arrives on.  The bounded wait gives up after `limit_ms`, records error
+ * code 9 and the kernel returns; *code receives the device error word. */
+int cn_selftest_bounded_wait(int limit_ms, int* code);
 
 /* ---- plumbing for hosts without a CUDA binding (ctypes callers) ------- */
 int cn_dev_alloc(void** ptr, size_t bytes, int device);
