@@ -42,25 +42,21 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 }
 __device__ __forceinline__ uint32_t pack_h2(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// grid (clips * heads), 192 threads.  qkv f16 [B*T][3d] (q | k | v), out f16 [B*T][d].
+// Stage K, V (all kAttnRows rows) and Q rows [q0, q0 + nq) of (clip b, head h)
+// into shared memory (rows >= T zeroed); nthr threads starting at thread index
+// tid take part.  The caller waits (cp_async_wait_all) and synchronises its
+// thread group afterwards.
 template <int HD>
-__global__ void __launch_bounds__(kAttnWarps * 32) k_attention_mma(const __half* __restrict__ qkv,
-                                                                    __half* __restrict__ out, int T, int d,
-                                                                    int heads) {
+__device__ __forceinline__ void attention_stage(const __half* __restrict__ qkv, __half* Qs, int T, int d, int b, int h,
+                                                int q0, int nq, int tid, int nthr) {
   constexpr int LD = HD + 8;  // halves; +16 B per row spreads ldmatrix rows over the banks
-  constexpr int NB = kAttnRows / 8;
   constexpr int CPR = HD / 8;  // 16-byte chunks per row
-  extern __shared__ __align__(16) uint8_t attn_smem[];
-  __half* Qs = reinterpret_cast<__half*>(attn_smem);
-  __half* Ks = Qs + kAttnRows * LD;
-  __half* Vs = Ks + kAttnRows * LD;
-  pdl_trigger();
-  pdl_wait();
-  const int b = blockIdx.x / heads, h = blockIdx.x % heads;
   const size_t ld = 3 * (size_t)d;
   const __half* base = qkv + (size_t)b * T * ld + (size_t)h * HD;
-  for (int i = threadIdx.x; i < 3 * kAttnRows * CPR; i += kAttnWarps * 32) {
-    const int mat = i / (kAttnRows * CPR), rem = i % (kAttnRows * CPR);
+  const int nkv = 2 * kAttnRows * CPR;
+  for (int i = tid; i < nkv + nq * CPR; i += nthr) {
+    const int mat = i < nkv ? 1 + i / (kAttnRows * CPR) : 0;
+    const int rem = i < nkv ? i % (kAttnRows * CPR) : i - nkv + q0 * CPR;
     const int r = rem / CPR, c = (rem % CPR) * 8;
     __half* dst = Qs + mat * kAttnRows * LD + r * LD + c;
     if (r < T)
@@ -68,12 +64,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention_mma(const __half*
     else
       *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
   }
-  cp_async_wait_all();
-  __syncthreads();
+}
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// One warp (wid in [0, 6)) computes query rows [16*wid, 16*wid+16) of the
+// staged (clip b, head h) and stores the valid rows of out f16 [B*T][d].
+template <int HD>
+__device__ __forceinline__ void attention_rows(const __half* Qs, __half* __restrict__ out, int T, int d, int b, int h,
+                                               int wid, int lane) {
+  constexpr int LD = HD + 8;
+  constexpr int NB = kAttnRows / 8;
+  const __half* Ks = Qs + kAttnRows * LD;
+  const __half* Vs = Ks + kAttnRows * LD;
   const int g = lane >> 2, t4 = lane & 3;
-  const int r0 = warp * 16;
+  const int r0 = wid * 16;
   // ---- S = Q K^T (16 rows x 96 keys per warp)
   float s[NB][4];
 #pragma unroll
@@ -169,6 +172,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention_mma(const __half*
     if (ra < T) *reinterpret_cast<__half2*>(oa + col) = __floats2half2_rn(o[nb][0], o[nb][1]);
     if (rb < T) *reinterpret_cast<__half2*>(ob + col) = __floats2half2_rn(o[nb][2], o[nb][3]);
   }
+}
+
+// grid (clips * heads), 192 threads.  qkv f16 [B*T][3d] (q | k | v), out f16 [B*T][d].
+template <int HD>
+__global__ void __launch_bounds__(kAttnWarps * 32) k_attention_mma(const __half* __restrict__ qkv,
+                                                                    __half* __restrict__ out, int T, int d,
+                                                                    int heads) {
+  extern __shared__ __align__(16) uint8_t attn_smem[];
+  __half* Qs = reinterpret_cast<__half*>(attn_smem);
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x / heads, h = blockIdx.x % heads;
+  attention_stage<HD>(qkv, Qs, T, d, b, h, 0, kAttnRows, threadIdx.x, kAttnWarps * 32);
+  cp_async_wait_all();
+  __syncthreads();
+  attention_rows<HD>(Qs, out, T, d, b, h, threadIdx.x >> 5, threadIdx.x & 31);
 }
 
 }  // namespace

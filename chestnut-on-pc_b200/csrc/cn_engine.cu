@@ -9,6 +9,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <mutex>
@@ -19,6 +20,7 @@
 #include "cn_common.cuh"
 #include "cn_gemm.cuh"
 #include "cn_ops.cuh"
+#include "cn_trunk.cuh"
 
 namespace cn {
 
@@ -145,6 +147,13 @@ struct cn_engine {
   __half *a0, *gat[5], *y3[5], *act[5];
   __half *cond16, *feat16, *h, *qkv, *att, *u, *pooled, *hid16, *z;
   float *condv, *x, *out;
+  // persistent trunk (single-clip frames): split-K partials + counter block
+  bool use_trunk = false;
+  int nsm = 0;
+  TrunkPlan trunk;
+  float* part = nullptr;
+  uint8_t* tctr = nullptr;
+  size_t tctr_bytes = 0;
   std::vector<Step> steps;
   std::vector<GemmPlan> plans;
   cudaGraph_t graph = nullptr;
@@ -262,6 +271,11 @@ static int layout_acts(cn_engine* e) {
   want((void**)&e->hid16, (size_t)B * kFeat * 2);
   want((void**)&e->z, (size_t)B * kTrunk * 2);
   want((void**)&e->out, (size_t)B * kNOut * 4);
+  if (e->use_trunk) {
+    want((void**)&e->part, trunk_part_floats((int)R, m.d, m.mlp, m.layers, e->nsm) * 4);
+    e->tctr_bytes = trunk_counter_bytes(m.layers);
+    want((void**)&e->tctr, e->tctr_bytes);
+  }
   for (auto& r : req) off += align256(r.second);
   e->abytes = off;
   CN_CUDA(cudaMalloc((void**)&e->ablob, e->abytes));
@@ -416,7 +430,35 @@ static int build_plan(cn_engine* e) {
                     ep));
   }
   // transformer
-  for (int l = 0; l < m.layers; ++l) {
+  if (e->use_trunk) {
+    const char* wn[4] = {".qkv.w", ".o.w", ".fc1.w", ".fc2.w"};
+    const char* bn[4] = {".qkv.b", ".o.b", ".fc1.b", ".fc2.b"};
+    const void* w0[4];
+    const float* b0[4];
+    long long wstride = 0, bstride = 0;
+    for (int g = 0; g < 4; ++g) {
+      w0[g] = wptr(e, std::string("l0") + wn[g]);
+      b0[g] = (const float*)wptr(e, std::string("l0") + bn[g]);
+    }
+    if (m.layers > 1) {
+      wstride = (long long)((uint8_t*)wptr(e, std::string("l1") + wn[0]) - (uint8_t*)w0[0]);
+      bstride = (long long)((const float*)wptr(e, std::string("l1") + bn[0]) - b0[0]);
+    }
+    for (int l = 0; l < m.layers; ++l)
+      for (int g = 0; g < 4; ++g) {
+        const std::string pre = "l" + std::to_string(l);
+        if ((uint8_t*)wptr(e, pre + wn[g]) != (uint8_t*)w0[g] + l * wstride ||
+            (const float*)wptr(e, pre + bn[g]) != b0[g] + l * bstride) {
+          set_last_error("trunk: layer tensors are not equally strided");
+          return CN_ERR_ARG;
+        }
+      }
+    CN_TRY(trunk_plan(&e->trunk, B, kT, m.d, m.mlp, m.heads, m.layers, w0, wstride, b0, bstride, e->x, e->h, e->qkv,
+                      e->att, e->u, e->part, e->tctr, e->rings.ctr, e->nsm));
+    e->steps.push_back({"trunk", [e](cudaStream_t s) { return trunk_launch(e->trunk, s); },
+                        kinfo("transformer_trunk", dim3(e->trunk.grid), dim3(256), dim3(1, 1, 1), e->trunk.smem)});
+  }
+  for (int l = 0; l < (e->use_trunk ? 0 : m.layers); ++l) {
     const std::string pre = "l" + std::to_string(l);
     int* bump = l == 0 ? e->rings.ctr : nullptr;  // all readers of the frame counter ran before this
     {
@@ -621,6 +663,13 @@ int cn_engine_create(const cn_config* cfg, cn_engine** out) {
     if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
       set_last_error("stream create failed"); r = CN_ERR_CUDA; break;
     }
+    // Single-clip frames run the transformer as one persistent kernel;
+    // CN_TRUNK=0 selects the per-layer kernels instead.
+    e->nsm = prop.multiProcessorCount;
+    {
+      const char* tv = getenv("CN_TRUNK");
+      e->use_trunk = trunk_supported(e->B * kT, e->m.d, e->m.heads) && !(tv && tv[0] == '0');
+    }
     layout_weights(e);
     if (cudaMalloc((void**)&e->wblob, e->wbytes) != cudaSuccess) {
       set_last_error("cudaMalloc of %zu weight bytes failed", e->wbytes); r = CN_ERR_CUDA; break;
@@ -763,6 +812,7 @@ int cn_reset_state(cn_engine* e) {
   CN_CUDA(cudaMemsetAsync(e->rings.desire, 0, (size_t)e->B * kDesireQ * kDesire * 4, e->stream));
   CN_CUDA(cudaMemsetAsync(e->rings.ctr, 0, sizeof(int), e->stream));
   CN_CUDA(cudaMemsetAsync(e->out, 0, (size_t)e->B * kNOut * 4, e->stream));
+  if (e->tctr) CN_CUDA(cudaMemsetAsync(e->tctr, 0, e->tctr_bytes, e->stream));
   CN_CUDA(cudaStreamSynchronize(e->stream));
   return 0;
 }

@@ -4,4 +4,5 @@
 #include "cn_reduce.cu"
 #include "cn_ops.cu"
 #include "cn_attn.cu"
+#include "cn_trunk.cu"
 #include "cn_engine.cu"

@@ -173,34 +173,27 @@ __global__ void k_gather_s2(const __half* __restrict__ act, int G, int B, int Hi
 }
 
 // ------------------------------------------------------------ layer norm
-// 4 warps per row (each a quarter of the row), 2 rows per 256-thread block;
-// per-warp partial sums are combined in warp order, so the result is
-// deterministic.  NV = float4 per lane, d = NV * 512.
-template <int NV>
-__global__ void __launch_bounds__(256) k_layernorm(const float* __restrict__ x, __half* __restrict__ y, int rows,
-                                                   int* bump) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ float part[2][4][2];
+// One row (d = NV * 512) by 4 warps, warp q owning the q-th quarter; per-warp
+// partial sums are combined in warp order, so the result is deterministic.
+// part[4][2] is shared scratch of the 4 warps and sync() synchronises them.
+// Rows with live == false take part in the synchronisation only.
+template <int NV, typename Sync>
+__device__ __forceinline__ void ln_row(const float* __restrict__ x, __half* __restrict__ y, int row, bool live, int q,
+                                       int lane, float (*part)[2], Sync sync) {
   constexpr int d = NV * 512;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int slot = warp >> 2, q = warp & 3;
-  const int row = blockIdx.x * 2 + slot;
-  if (bump && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(bump, 1);
-  const bool live = row < rows;
   const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(live ? row : 0) * d + q * (d / 4));
   float4 v[NV];
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    v[i] = live ? xr[lane + 32 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    v[i] = live ? __ldcg(xr + lane + 32 * i) : make_float4(0.f, 0.f, 0.f, 0.f);  // L2: rows written by other SMs
     s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) part[slot][q][0] = s;
-  __syncthreads();
-  const float mean = (((part[slot][0][0] + part[slot][1][0]) + part[slot][2][0]) + part[slot][3][0]) / (float)d;
+  if (lane == 0) part[q][0] = s;
+  sync();
+  const float mean = (((part[0][0] + part[1][0]) + part[2][0]) + part[3][0]) / (float)d;
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
@@ -209,9 +202,9 @@ __global__ void __launch_bounds__(256) k_layernorm(const float* __restrict__ x, 
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) part[slot][q][1] = ss;
-  __syncthreads();
-  const float var = (((part[slot][0][1] + part[slot][1][1]) + part[slot][2][1]) + part[slot][3][1]) / (float)d;
+  if (lane == 0) part[q][1] = ss;
+  sync();
+  const float var = (((part[0][1] + part[1][1]) + part[2][1]) + part[3][1]) / (float)d;
   const float rstd = 1.0f / sqrtf(var + 1e-5f);
   if (!live) return;
   uint2* yr = reinterpret_cast<uint2*>(y + (size_t)row * d + q * (d / 4));
@@ -224,6 +217,20 @@ __global__ void __launch_bounds__(256) k_layernorm(const float* __restrict__ x, 
     u.y = *reinterpret_cast<uint32_t*>(&h1);
     yr[lane + 32 * i] = u;
   }
+}
+
+// 2 rows per 256-thread block.
+template <int NV>
+__global__ void __launch_bounds__(256) k_layernorm(const float* __restrict__ x, __half* __restrict__ y, int rows,
+                                                   int* bump) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float part[2][4][2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slot = warp >> 2, q = warp & 3;
+  const int row = blockIdx.x * 2 + slot;
+  if (bump && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(bump, 1);
+  ln_row<NV>(x, y, row, row < rows, q, lane, part[slot], [] { __syncthreads(); });
 }
 
 constexpr int kTP = 96;  // max tokens per clip handled by the pooling kernels

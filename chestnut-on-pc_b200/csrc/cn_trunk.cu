@@ -1,0 +1,788 @@
+// Persistent transformer trunk for single-clip frames (M <= 128 token rows).
+//
+// The 1B frame's transformer streams 100 MB of f16 weights per layer against
+// 88 tokens of activations, so it is an HBM stream with small dependent steps
+// in between.  Launched as separate kernels, every GEMM pays its launch,
+// pipeline fill and split-K epilogue before its successor can touch HBM.  This
+// kernel runs the whole trunk (layers x {LN1, QKV, attention, O + residual,
+// LN2, fc1 + GELU, fc2 + residual}) as one cooperative launch of one CTA per
+// SM, with a grid barrier between dependent phases, and decouples the weight
+// stream from the phases:
+//
+//   warp 0 (lane 0)  streams every weight k-block this CTA will consume, over
+//                    all layers, into a ring of shared-memory stages with TMA.
+//                    It waits only for free stages, never for phase barriers,
+//                    so HBM keeps streaming through barriers, LayerNorms and
+//                    attention.
+//   warps 1..7       the compute group.  In a GEMM phase warp 1 lane 0 loads
+//                    the activation k-blocks (TMA, after the barrier), warp 2
+//                    lane 0 issues tcgen05.mma and warps 4..7 run the
+//                    epilogue (TMEM lane quadrants 0..3).  LayerNorm uses
+//                    warps 4..7 (4 warps per row), attention warps 1..6.
+//
+// GEMMs are computed transposed ("swap AB"): D[128 features][ntok tokens] =
+// W[128 x 64k] (A, the k-blocked weight tile) x X[ntok x 64k]^T (B), M = 128,
+// N = ntok (88 tokens -> 96), f32 accumulator in TMEM.  A GEMM slot is cut
+// into units (128-feature tile, split-K part); a unit with S > 1 writes its
+// partial tile to an L2-resident scratch, the S units of a feature tile meet
+// on an arrival counter, and unit s then reduces tokens [s*M/S, (s+1)*M/S) in
+// split order 0..S-1 (deterministic) and applies bias / GELU / residual.
+//
+// Every wait is bounded (%globaltimer); on timeout a code lands in the device
+// error word and the kernel unwinds instead of hanging.  Counters are
+// monotonic across launches (targets derive from a launch epoch), so nothing
+// has to be reset between frames.  No TMA multicast.
+#include <algorithm>
+
+#include "cn_common.cuh"
+#include "cn_gemm.cuh"
+#include "cn_ops.cuh"
+#include "cn_trunk.cuh"
+
+namespace cn {
+
+namespace {
+
+constexpr int kTrThreads = 256;
+constexpr int kComputeThreads = 192;       // warps 2..7
+constexpr int kComputeT0 = 64;             // first compute thread
+constexpr int kWTileBytes = 128 * 64 * 2;  // one k-block of 128 output features
+constexpr int kBarCompute = 1, kBarEpi = 2;
+constexpr int kPhasesPerLayer = 7;
+constexpr int kMaxTrunkSplit = 16;
+constexpr int kMaxTiles = 64;  // feature tiles per GEMM slot (N <= 8192)
+
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+// Generic-proxy global writes of this thread -> visible to async-proxy (TMA) reads.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool dev_error_set() { return *reinterpret_cast<volatile int*>(&g_cn_dev_error) != 0; }
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Prefetch one weight tile (4-D k-blocked map) into L2; no completion tracking.
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+// Shared -> global tiled store (no multicast), tracked by the bulk async-group.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_and_wait() {
+  asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Spin until *ctr >= target (bounded).  false on timeout or a recorded error.
+template <typename T, typename Ld>
+__device__ __forceinline__ bool spin_until(const T* ctr, T target, int code, Ld ld) {
+  if (ld(ctr) >= target) return true;
+  const unsigned long long t0 = global_ns();
+  while (ld(ctr) < target) {
+    if (dev_error_set()) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      set_dev_error(code);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Grid barrier of the compute groups (all compute threads call it).
+__device__ __forceinline__ bool grid_sync(unsigned long long* ctr, unsigned long long target, volatile int* flag) {
+  fence_proxy_async_global();
+  named_sync(kBarCompute, kComputeThreads);
+  if (threadIdx.x == kComputeT0) {
+    // one release per CTA covers the group's writes (ordered by the barrier above)
+    fence_acq_rel_gpu();
+    red_release_add(ctr, 1ull);
+    bool ok = spin_until(ctr, target, 10, ld_acquire_u64);
+    fence_acq_rel_gpu();
+    *flag = ok && !dev_error_set();
+  }
+  named_sync(kBarCompute, kComputeThreads);
+  return *flag != 0;
+}
+
+__device__ __forceinline__ void unit_range(const TrunkArgs& a, int gi, int u, int* nt, int* s, int* kb0, int* kb1) {
+  const int S = a.S[gi], KB = a.K[gi] / 64;
+  *nt = u / S;
+  *s = u % S;
+  *kb0 = *s * KB / S;
+  *kb1 = (*s + 1) * KB / S;
+}
+
+// Final value of output (token t, feature n) of GEMM slot gi.
+__device__ __forceinline__ void store_out(const TrunkArgs& a, int gi, int t, int n, float v) {
+  const size_t i = (size_t)t * a.N[gi] + n;
+  if (gi == TG_QKV) {
+    a.qkv[i] = __float2half_rn(v);
+  } else if (gi == TG_FC1) {
+    a.u[i] = __float2half_rn(apply_act(v, ACT_GELU));
+  } else {
+    float* px = a.x + i;
+    *px = __ldcg(px) + v;
+  }
+}
+
+// Same for features n..n+3 (n % 4 == 0); old = the residual rows (O, fc2).
+__device__ __forceinline__ void store_out4(const TrunkArgs& a, int gi, int t, int n, float4 v, float4 old) {
+  const size_t i = (size_t)t * a.N[gi] + n;
+  if (gi == TG_QKV || gi == TG_FC1) {
+    const bool g = gi == TG_FC1;
+    __align__(8) __half hv[4] = {__float2half_rn(g ? apply_act(v.x, ACT_GELU) : v.x),
+                                 __float2half_rn(g ? apply_act(v.y, ACT_GELU) : v.y),
+                                 __float2half_rn(g ? apply_act(v.z, ACT_GELU) : v.z),
+                                 __float2half_rn(g ? apply_act(v.w, ACT_GELU) : v.w)};
+    *reinterpret_cast<uint2*>((g ? a.u : a.qkv) + i) = *reinterpret_cast<const uint2*>(hv);
+  } else {
+    *reinterpret_cast<float4*>(a.x + i) = make_float4(old.x + v.x, old.y + v.y, old.z + v.z, old.w + v.w);
+  }
+}
+
+// Attention of query rows [q0, q0 + 16) of (clip b, head h).  Shared layout
+// (halves, row stride HD + 8): Q rows 0..15, K rows 16..111, V rows 112..207.
+constexpr int kAttnKW = 32;                  // keys per warp
+constexpr int kAttnWarpsT = kAttnRows / kAttnKW;  // 3 warps split the keys
+
+template <int HD>
+__device__ __forceinline__ void attn16_stage(const __half* __restrict__ qkv, __half* base, int T, int d, int b, int h,
+                                             int q0, int tid, int nthr) {
+  constexpr int LD = HD + 8, CPR = HD / 8;
+  const size_t ld = 3 * (size_t)d;
+  const __half* src = qkv + (size_t)b * T * ld + (size_t)h * HD;
+  for (int i = tid; i < (16 + 2 * kAttnRows) * CPR; i += nthr) {
+    const int row = i / CPR, c = (i % CPR) * 8;
+    const int mat = row < 16 ? 0 : (row < 16 + kAttnRows ? 1 : 2);
+    const int r = mat == 0 ? q0 + row : row - 16 - (mat - 1) * kAttnRows;
+    __half* dst = base + row * LD + c;
+    if (r < T)
+      cp_async16(dst, src + (size_t)r * ld + (size_t)mat * d + c);
+    else
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Warp w: scores of the 16 rows against keys [32w, 32w+32), their row max m
+// and sum l of exp(s - m), and O_w = exp(S - m) V_w (P split f16 hi + lo).
+// Results go to shared memory over the (no longer needed) Q/K rows:
+// float O[3][16][HD], then float ml[3][16][2].
+template <int HD>
+__device__ __forceinline__ void attn16_keys(__half* base, int T, int w, int lane) {
+  constexpr int LD = HD + 8;
+  const __half* Qs = base;
+  const __half* Ks = base + 16 * LD;
+  const __half* Vs = base + (16 + kAttnRows) * LD;
+  const int g = lane >> 2, t4 = lane & 3;
+  float s[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < HD; kk += 16) {
+    uint32_t a[4];
+    {
+      const int i = lane >> 3;
+      ldsm_x4(a, Qs + ((i & 1) * 8 + (lane & 7)) * LD + kk + (i >> 1) * 8);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t bb[2];
+      ldsm_x2(bb, Ks + (kAttnKW * w + 8 * j + (lane & 7)) * LD + kk + ((lane >> 3) & 1) * 8);
+      mma16816(s[j], a, bb[0], bb[1]);
+    }
+  }
+  const float scale = 1.0f / sqrtf((float)HD);
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const bool valid = kAttnKW * w + 8 * j + 2 * t4 + e < T;
+      s[j][e] = valid ? s[j][e] * scale : -INFINITY;
+      s[j][2 + e] = valid ? s[j][2 + e] * scale : -INFINITY;
+      m0 = fmaxf(m0, s[j][e]);
+      m1 = fmaxf(m1, s[j][2 + e]);
+    }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+  }
+  float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      s[j][e] = m0 == -INFINITY ? 0.f : expf(s[j][e] - m0);
+      s[j][2 + e] = m1 == -INFINITY ? 0.f : expf(s[j][2 + e] - m1);
+      l0 += s[j][e];
+      l1 += s[j][2 + e];
+    }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+  float o[HD / 8][4];
+#pragma unroll
+  for (int nb = 0; nb < HD / 8; ++nb) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < kAttnKW / 16; ++ks) {
+    uint32_t ahi[4], alo[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int j = 2 * ks + (q >> 1);
+      const float x = s[j][(q & 1) * 2], y = s[j][(q & 1) * 2 + 1];
+      const __half2 hi = __floats2half2_rn(x, y);
+      const float2 hf = __half22float2(hi);
+      ahi[q] = pack_h2(hi);
+      alo[q] = pack_h2(__floats2half2_rn(x - hf.x, y - hf.y));
+    }
+#pragma unroll
+    for (int nb = 0; nb < HD / 8; nb += 2) {
+      uint32_t bv[4];
+      const int i = lane >> 3;
+      ldsm_x4_t(bv, Vs + (kAttnKW * w + 16 * ks + (i & 1) * 8 + (lane & 7)) * LD + 8 * nb + (i >> 1) * 8);
+      mma16816(o[nb], ahi, bv[0], bv[1]);
+      mma16816(o[nb], alo, bv[0], bv[1]);
+      mma16816(o[nb + 1], ahi, bv[2], bv[3]);
+      mma16816(o[nb + 1], alo, bv[2], bv[3]);
+    }
+  }
+  // every warp is done with Q and K before they are overwritten
+  named_sync(kBarCompute, kComputeThreads);
+  float* O = reinterpret_cast<float*>(base) + (size_t)w * 16 * HD;
+#pragma unroll
+  for (int nb = 0; nb < HD / 8; ++nb) {
+    const int col = 8 * nb + 2 * t4;
+    *reinterpret_cast<float2*>(O + g * HD + col) = make_float2(o[nb][0], o[nb][1]);
+    *reinterpret_cast<float2*>(O + (g + 8) * HD + col) = make_float2(o[nb][2], o[nb][3]);
+  }
+  float* ml = reinterpret_cast<float*>(base) + kAttnWarpsT * 16 * HD + w * 32;
+  if (t4 == 0) {
+    ml[2 * g] = m0;
+    ml[2 * g + 1] = l0;
+    ml[2 * (g + 8)] = m1;
+    ml[2 * (g + 8) + 1] = l1;
+  }
+}
+
+// Combine the 3 key blocks and store rows [q0, q0+16) of out f16 [B*T][d].
+template <int HD>
+__device__ __forceinline__ void attn16_combine(const __half* base, __half* __restrict__ out, int T, int d, int b, int h,
+                                               int q0, int tid, int nthr) {
+  const float* O = reinterpret_cast<const float*>(base);
+  const float* ml = O + kAttnWarpsT * 16 * HD;
+  for (int i = tid; i < 16 * HD / 4; i += nthr) {
+    const int r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+    if (q0 + r >= T) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarpsT; ++w) M = fmaxf(M, ml[w * 32 + 2 * r]);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kAttnWarpsT; ++w) {
+      const float mw = ml[w * 32 + 2 * r];
+      const float f = mw == -INFINITY ? 0.f : expf(mw - M);
+      L += f * ml[w * 32 + 2 * r + 1];
+      const float4 v = *reinterpret_cast<const float4*>(O + ((size_t)w * 16 + r) * HD + c);
+      acc.x += f * v.x; acc.y += f * v.y; acc.z += f * v.z; acc.w += f * v.w;
+    }
+    __align__(8) __half hv[4] = {__float2half_rn(acc.x / L), __float2half_rn(acc.y / L), __float2half_rn(acc.z / L),
+                                 __float2half_rn(acc.w / L)};
+    *reinterpret_cast<uint2*>(out + ((size_t)b * T + q0 + r) * d + (size_t)h * HD + c) = *reinterpret_cast<uint2*>(hv);
+  }
+}
+
+size_t attn16_smem_bytes(int hd) { return (size_t)(16 + 2 * kAttnRows) * (hd + 8) * 2; }
+
+template <int HD, int NV>
+__global__ void __launch_bounds__(kTrThreads, 1)
+    k_trunk(const __grid_constant__ TrunkMaps maps, const __grid_constant__ TrunkArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int ST = a.stages;
+  uint64_t* fullW = reinterpret_cast<uint64_t*>(smem + a.bar_off);
+  uint64_t* fullX = fullW + 8;
+  uint64_t* empty = fullW + 16;
+  uint64_t* done = fullW + 24;
+  uint64_t* fixb = fullW + 25;  // reduction slices landed
+  uint64_t* rbar = fullW + 26;  // residual rows landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fullW + 27);
+  volatile int* flags = reinterpret_cast<volatile int*>(fullW + 28);  // [0] grid barrier, [1] tile counter
+  float(*lnpart)[2] = reinterpret_cast<float(*)[2]>(fullW + 30);     // 4 x 2 floats
+  uint8_t* aux = smem + a.aux_off;  // attention staging / split-K reduction (phases never overlap)
+  __half* attn = reinterpret_cast<__half*>(aux);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&fullW[s], 1);
+      mbar_init(&fullX[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    mbar_init(fixb, 1);
+    mbar_init(rbar, 1);
+    fence_barrier_init();
+    for (int g = 0; g < 4; ++g) {
+      tma_prefetch_desc(&maps.w[g]);
+      tma_prefetch_desc(&maps.x[g]);
+      tma_prefetch_desc(&maps.p[g]);
+    }
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const unsigned epoch = *reinterpret_cast<volatile unsigned*>(a.epoch);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.bump) atomicAdd(a.bump, 1);
+
+  if (warp < 2) {
+    // ------------------------------------------------ weight stream
+    // Two issuing warps (k-blocks alternate between them): a thread's TMA
+    // loads complete one after another, so throughput scales with issuers.
+    if (lane == 0) {
+      uint32_t g = 0, last = 0;
+      bool ok = true;
+      for (int l = 0; l < a.layers && ok; ++l)
+        for (int gi = 0; gi < 4 && ok; ++gi) {
+          if ((int)blockIdx.x >= a.units[gi]) continue;
+          int nt, s, kb0, kb1;
+          unit_range(a, gi, blockIdx.x, &nt, &s, &kb0, &kb1);
+          if (warp == 0) {
+            // L2 look-ahead: request this CTA's next unit from HBM now.
+            for (int l2 = l, g2 = gi + 1; l2 < a.layers; ++g2) {
+              if (g2 == 4) {
+                g2 = -1;
+                ++l2;
+                continue;
+              }
+              if ((int)blockIdx.x >= a.units[g2]) continue;
+              int nt2, s2, k0, k1;
+              unit_range(a, g2, blockIdx.x, &nt2, &s2, &k0, &k1);
+              for (int kb = k0; kb < k1; ++kb) tma_prefetch_l2_4d(&maps.w[g2], 0, nt2 * 128, kb, l2);
+              break;
+            }
+          }
+          for (int kb = kb0; kb < kb1; ++kb, ++g) {
+            if ((int)(g & 1) != warp) continue;
+            const int st = (int)(g % ST);
+            const uint32_t ph = (g / ST) & 1;
+            if (!mbar_wait(&empty[st], ph ^ 1, 14)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&fullW[st], kWTileBytes);
+            tma_load_4d(smem + st * a.stage_bytes, &maps.w[gi], &fullW[st], 0, nt * 128, kb, l);
+            last = g + 1;
+          }
+        }
+      if (!ok || dev_error_set()) {
+        // do not leave a TMA write in flight into shared memory of an exiting CTA
+        for (uint32_t i = last > (uint32_t)ST ? last - ST : 0; i < last; ++i)
+          if ((int)(i & 1) == warp) mbar_wait(&fullW[i % ST], (i / ST) & 1, 0, 100000000ull);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ compute group (warps 2..7)
+    const int ct = threadIdx.x - kComputeT0;
+    uint32_t gx = 0, gm = 0, ndone = 0, nfix = 0, nres = 0, x_last = 0;
+    unsigned long long bar_idx = (unsigned long long)epoch * a.phases;
+    const unsigned long long nb = gridDim.x;
+    bool ok = true;
+    for (int l = 0; l < a.layers && ok; ++l) {
+      for (int ph = 0; ph < kPhasesPerLayer && ok; ++ph) {
+        if (ph == 0 || ph == 4) {
+          // ---------------- LayerNorm (x -> h), warps 4..7, one row at a time
+          if (warp >= 4)
+            for (int r = blockIdx.x; r < a.M; r += gridDim.x)
+              ln_row<NV>(a.x, a.h, r, true, warp & 3, lane, lnpart, [] { named_sync(kBarEpi, 128); });
+        } else if (ph == 2) {
+          // ---------------- attention, one (clip, head, 16 query rows) per CTA
+          const int QB = (a.T + 15) / 16;
+          const int units = a.B * a.heads * QB;
+          for (int uu = blockIdx.x; uu < units; uu += gridDim.x) {
+            const int qb = uu % QB, h = (uu / QB) % a.heads, b = uu / (QB * a.heads);
+            attn16_stage<HD>(a.qkv, attn, a.T, a.d, b, h, 16 * qb, ct, kComputeThreads);
+            cp_async_wait_all();
+            named_sync(kBarCompute, kComputeThreads);
+            if (warp < 2 + kAttnWarpsT)
+              attn16_keys<HD>(attn, a.T, warp - 2, lane);
+            else
+              named_sync(kBarCompute, kComputeThreads);  // pairs with the one inside attn16_keys
+            named_sync(kBarCompute, kComputeThreads);
+            attn16_combine<HD>(attn, a.att, a.T, a.d, b, h, 16 * qb, ct, kComputeThreads);
+            named_sync(kBarCompute, kComputeThreads);
+          }
+        } else {
+          // ---------------- GEMM slot
+          const int gi = ph == 1 ? TG_QKV : (ph == 3 ? TG_O : (ph == 5 ? TG_FC1 : TG_FC2));
+          if ((int)blockIdx.x < a.units[gi]) {
+            int nt, s, kb0, kb1;
+            unit_range(a, gi, blockIdx.x, &nt, &s, &kb0, &kb1);
+            const int nkb = kb1 - kb0;
+            const int S = a.S[gi], M = a.M, R = a.R[gi];
+            const int t0 = s * M / S, t1 = (s + 1) * M / S;
+            const bool resid = S > 1 && (gi == TG_O || gi == TG_FC2);
+            // residual rows [t0, t0 + R) of this tile sit after the staging / slice rows
+            uint8_t* xres = aux + (size_t)(M > S * R ? M : S * R) * 512;
+            if (warp == 2 || warp == 3) {
+              // activation k-blocks: warp 2 the even ones, warp 3 the odd ones
+              if (lane == 0) {
+                fence_proxy_async_global();
+                for (int i = 0; i < nkb; ++i, ++gx) {
+                  if ((int)(gx & 1) != warp - 2) continue;
+                  const int st = (int)(gx % ST);
+                  const uint32_t par = (gx / ST) & 1;
+                  if (!mbar_wait(&empty[st], par ^ 1, 12)) break;
+                  mbar_arrive_expect_tx(&fullX[st], (uint32_t)a.x_bytes);
+                  tma_load_2d(smem + st * a.stage_bytes + kWTileBytes, &maps.x[gi], &fullX[st], (kb0 + i) * 64, 0);
+                  x_last = gx + 1;
+                }
+              }
+              __syncwarp();
+            } else if (warp == 5 && resid) {
+              if (lane == 0) {
+                fence_proxy_async_global();
+                mbar_arrive_expect_tx(rbar, (uint32_t)R * 512u);
+                tma_load_2d(xres, &maps.r[gi], rbar, nt * 128, t0);
+              }
+              __syncwarp();
+            }
+            if (warp == 4 && lane == 0) {
+              tc_fence_after();
+              const uint32_t idesc = umma_idesc_f16(a.ntok, false);
+              for (int i = 0; i < nkb; ++i, ++gm) {
+                const int st = (int)(gm % ST);
+                const uint32_t par = (gm / ST) & 1;
+                if (!mbar_wait(&fullW[st], par, 13) || !mbar_wait(&fullX[st], par, 1)) break;
+                tc_fence_after();
+                const uint32_t wa = smem_u32(smem + st * a.stage_bytes);
+                const uint32_t xa = wa + kWTileBytes;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  tc_mma_f16(tmem, umma_desc_sw128(wa + k * 32, 16, 1024), umma_desc_sw128(xa + k * 32, 16, 1024),
+                             idesc, (i > 0 || k > 0) ? 1u : 0u);
+                tc_commit(&empty[st]);
+              }
+              tc_commit(done);
+            }
+            __syncwarp();
+            if (warp >= 4) {
+              const int e = threadIdx.x - 128;  // == 32 * (warp & 3) + lane: TMEM lane / feature in tile
+              const int n = nt * 128 + e;
+              const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+              const bool have = mbar_wait(done, ndone & 1, 15);
+              tc_fence_after();
+              if (S == 1) {
+                const float bv = a.bias[gi][(size_t)l * a.bias_lstride + n];
+                if (have)
+                  for (int c = 0; c < a.ntok; c += 16) {
+                    uint32_t r[16];
+                    tmem_ld16(taddr + c, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                      if (c + j < M) store_out(a, gi, c + j, n, __uint_as_float(r[j]) + bv);
+                  }
+                tc_fence_before();
+              } else {
+                // partial tile -> shared staging -> one TMA store; the S units of
+                // this feature tile meet on an arrival counter; unit s then
+                // reduces tokens [t0, t1) from one TMA box holding all S
+                // partials (split order 0..S-1) on the whole compute group.
+                float* stg = reinterpret_cast<float*>(aux);
+                if (have)
+                  for (int c0 = 0; c0 < a.ntok; c0 += 64) {
+                    uint32_t r[4][16];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                      if (c0 + 16 * q < a.ntok) tmem_ld16(taddr + c0 + 16 * q, r[q]);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+#pragma unroll
+                      for (int j = 0; j < 16; ++j)
+                        if (c0 + 16 * q + j < M) stg[(c0 + 16 * q + j) * 128 + e] = __uint_as_float(r[q][j]);
+                  }
+                tc_fence_before();
+                fence_proxy_async_smem();
+                named_sync(kBarEpi, 128);
+                if (e == 0) {
+                  if (have) {
+                    tma_store_3d(&maps.ps[gi], stg, nt * 128, 0, s);
+                    bulk_commit_and_wait();  // written, and the staging tile is free again
+                  }
+                  fence_proxy_async_global();
+                  unsigned* ctr = a.tile_ctr + ((size_t)l * 4 + gi) * kMaxTiles + nt;
+                  fence_acq_rel_gpu();
+                  red_release_add(ctr, 1u);
+                  const bool met = spin_until(ctr, (unsigned)S * (epoch + 1u), 11, ld_acquire_u32);
+                  fence_acq_rel_gpu();
+                  fence_proxy_async_global();
+                  flags[1] = met && have;
+                  if (met && have) {
+                    mbar_arrive_expect_tx(fixb, (uint32_t)(S * R) * 512u);
+                    tma_load_3d(aux, &maps.p[gi], fixb, nt * 128, t0, 0);
+                  }
+                }
+              }
+            }
+            if (S > 1) {
+              // the whole compute group reduces once the slices have landed
+              named_sync(kBarCompute, kComputeThreads);
+              bool landed = false;
+              if (flags[1]) {
+                landed = mbar_wait(fixb, nfix & 1, 16);
+                ++nfix;
+              }
+              if (resid) {
+                landed = mbar_wait(rbar, nres & 1, 17) && landed;
+                ++nres;
+              }
+              if (landed) {
+                const float* bias = a.bias[gi] + (size_t)l * a.bias_lstride + nt * 128;
+                for (int i = ct; i < (t1 - t0) * 32; i += kComputeThreads) {
+                  const int tt = i >> 5, fq = i & 31;
+                  const float* row = reinterpret_cast<const float*>(aux) + tt * 128 + 4 * fq;
+                  float4 acc = *reinterpret_cast<const float4*>(row);
+                  for (int q = 1; q < S; ++q) {
+                    const float4 v = *reinterpret_cast<const float4*>(row + (size_t)q * R * 128);
+                    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                  }
+                  const float4 b4 = *reinterpret_cast<const float4*>(bias + 4 * fq);
+                  acc.x += b4.x; acc.y += b4.y; acc.z += b4.z; acc.w += b4.w;
+                  const float4 old = resid ? *reinterpret_cast<const float4*>(
+                                                 reinterpret_cast<const float*>(xres) + tt * 128 + 4 * fq)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                  store_out4(a, gi, t0 + tt, nt * 128 + 4 * fq, acc, old);
+                }
+              }
+              // the staging area is reused only after the grid barrier
+            }
+            ++ndone;
+          }
+        }
+        ok = grid_sync(a.grid_ctr, (++bar_idx) * nb, &flags[0]);
+      }
+    }
+    if ((warp == 2 || warp == 3) && lane == 0 && !ok) {
+      for (uint32_t i = x_last > (uint32_t)ST ? x_last - ST : 0; i < x_last; ++i)
+        if ((int)(i & 1) == warp - 2) mbar_wait(&fullX[i % ST], (i / ST) & 1, 0, 100000000ull);
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, 128);
+  if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(a.epoch, 1u);
+}
+
+using TrunkFn = void (*)(TrunkMaps, TrunkArgs);
+
+TrunkFn trunk_kernel(int hd, int d) {
+  if (hd == 64 && d == 512) return reinterpret_cast<TrunkFn>(k_trunk<64, 1>);
+  if (hd == 128 && d == 2048) return reinterpret_cast<TrunkFn>(k_trunk<128, 4>);
+  if (hd == 64 && d == 1024) return reinterpret_cast<TrunkFn>(k_trunk<64, 2>);
+  if (hd == 128 && d == 1024) return reinterpret_cast<TrunkFn>(k_trunk<128, 2>);
+  return nullptr;
+}
+
+int trunk_split(int ntiles, int kb, int nsm) {
+  int s = nsm / ntiles;
+  if (s > kb) s = kb;
+  if (s > kMaxTrunkSplit) s = kMaxTrunkSplit;
+  return s < 1 ? 1 : s;
+}
+
+}  // namespace
+
+bool trunk_supported(int M, int d, int heads) {
+  return M > 0 && M <= 128 && heads > 0 && d % heads == 0 && trunk_kernel(d / heads, d) != nullptr;
+}
+
+size_t trunk_part_floats(int M, int d, int mlp, int layers, int nsm) {
+  (void)layers;
+  const int N[4] = {3 * d, d, mlp, d}, K[4] = {d, d, d, mlp};
+  size_t mx = 0;
+  for (int g = 0; g < 4; ++g) {
+    const size_t s = (size_t)trunk_split(N[g] / 128, K[g] / 64, nsm);
+    mx = std::max(mx, s * M * N[g]);
+  }
+  return mx;
+}
+
+size_t trunk_counter_bytes(int layers) { return 256 + (size_t)layers * 4 * kMaxTiles * sizeof(unsigned); }
+
+int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layers, const void* const w0[4],
+               long long w_lstride_bytes, const float* const b0[4], long long b_lstride, float* x, __half* h,
+               __half* qkv, __half* att, __half* u, float* part, void* counters, int* bump, int nsm) {
+  const int M = B * T;
+  if (!trunk_supported(M, d, heads) || T > 96 || (mlp % 128) || (d % 128) || mlp / 128 > kMaxTiles ||
+      3 * d / 128 > kMaxTiles || (w_lstride_bytes % 16)) {
+    set_last_error("trunk_plan: unsupported shape M=%d d=%d mlp=%d heads=%d", M, d, mlp, heads);
+    return -2;
+  }
+  memset(tp, 0, sizeof(*tp));
+  TrunkArgs& a = tp->a;
+  a.M = M;
+  a.ntok = (M + 15) / 16 * 16;
+  a.T = T;
+  a.B = B;
+  a.d = d;
+  a.mlp = mlp;
+  a.heads = heads;
+  a.layers = layers;
+  const int N[4] = {3 * d, d, mlp, d}, K[4] = {d, d, d, mlp};
+  for (int g = 0; g < 4; ++g) {
+    a.N[g] = N[g];
+    a.K[g] = K[g];
+    a.S[g] = trunk_split(N[g] / 128, K[g] / 64, nsm);
+    a.units[g] = N[g] / 128 * a.S[g];
+    a.bias[g] = b0[g];
+    if (a.units[g] > nsm) {  // every unit needs its own CTA (one CTA per SM)
+      set_last_error("trunk_plan: %d feature tiles exceed %d SMs", N[g] / 128, nsm);
+      return -2;
+    }
+    a.R[g] = (M + a.S[g] - 1) / a.S[g];
+  }
+  a.bias_lstride = b_lstride;
+  a.x_bytes = a.ntok * 128;
+  a.stage_bytes = kWTileBytes + a.x_bytes;  // both multiples of 1 KB (SW128 atoms)
+  tp->hd = d / heads;
+  // aux: attention staging, or the S reduction slices (+ residual rows) of a unit
+  // aux: attention staging, or (staging tile | S reduction slices) + residual rows
+  size_t aux_bytes = attn16_smem_bytes(tp->hd);
+  for (int g = 0; g < 4; ++g) {
+    const size_t rows = (size_t)std::max(M, a.S[g] * a.R[g]) + ((g == TG_O || g == TG_FC2) ? a.R[g] : 0);
+    aux_bytes = std::max(aux_bytes, rows * 512);
+  }
+  const size_t budget = 227 * 1024 - 1024 - 256;
+  if (aux_bytes + 2 * (size_t)a.stage_bytes > budget) {
+    set_last_error("trunk_plan: shared memory too small for the weight ring");
+    return -2;
+  }
+  int st = (int)((budget - aux_bytes) / a.stage_bytes);
+  if (st > 8) st = 8;
+  if (st < 2) {
+    set_last_error("trunk_plan: shared memory too small for the weight ring");
+    return -2;
+  }
+  a.stages = st;
+  a.aux_off = st * a.stage_bytes;
+  a.bar_off = (int)((a.aux_off + aux_bytes + 63) / 64 * 64);
+  a.phases = kPhasesPerLayer * layers;
+  tp->smem = (size_t)a.bar_off + 256 + 1024;
+  a.x = x;
+  a.h = h;
+  a.qkv = qkv;
+  a.att = att;
+  a.u = u;
+  a.part = part;
+  uint8_t* c = static_cast<uint8_t*>(counters);
+  a.grid_ctr = reinterpret_cast<unsigned long long*>(c);
+  a.epoch = reinterpret_cast<unsigned*>(c + 64);
+  a.tile_ctr = reinterpret_cast<unsigned*>(c + 256);
+  a.bump = bump;
+  tp->grid = nsm;
+  // tensor maps
+  for (int g = 0; g < 4; ++g) {
+    const uint64_t dims[4] = {64, (uint64_t)N[g], (uint64_t)(K[g] / 64), (uint64_t)layers};
+    const uint64_t strides[3] = {128, (uint64_t)N[g] * 128, (uint64_t)w_lstride_bytes};
+    const uint32_t box[4] = {64, 128, 1, 1};
+    if (encode(&tp->maps.w[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, w0[g], dims, strides, box,
+               CU_TENSOR_MAP_SWIZZLE_128B))
+      return -3;
+  }
+  const __half* xin[4] = {h, att, h, u};
+  for (int g = 0; g < 4; ++g) {
+    const uint64_t dims[2] = {(uint64_t)K[g], (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K[g] * 2};
+    const uint32_t box[2] = {64, (uint32_t)a.ntok};
+    if (encode(&tp->maps.x[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xin[g], dims, strides, box,
+               CU_TENSOR_MAP_SWIZZLE_128B))
+      return -3;
+  }
+  for (int g = 0; g < 4; ++g) {
+    const uint64_t dims[3] = {(uint64_t)N[g], (uint64_t)M, (uint64_t)a.S[g]};
+    const uint64_t strides[2] = {(uint64_t)N[g] * 4, (uint64_t)M * N[g] * 4};
+    const uint32_t box[3] = {128, (uint32_t)a.R[g], (uint32_t)a.S[g]};  // all S slices in one load
+    if (encode(&tp->maps.p[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, part, dims, strides, box,
+               CU_TENSOR_MAP_SWIZZLE_NONE))
+      return -3;
+    const uint32_t sbox[3] = {128, (uint32_t)M, 1};
+    if (encode(&tp->maps.ps[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, part, dims, strides, sbox,
+               CU_TENSOR_MAP_SWIZZLE_NONE))
+      return -3;
+    const uint64_t xd[2] = {(uint64_t)d, (uint64_t)M};
+    const uint64_t xs[1] = {(uint64_t)d * 4};
+    const uint32_t xb[2] = {128, (uint32_t)a.R[g]};
+    if (encode(&tp->maps.r[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, x, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return -3;
+  }
+  TrunkFn fn = trunk_kernel(tp->hd, d);
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tp->smem) != cudaSuccess) {
+    set_last_error("trunk_plan: cannot reserve %zu bytes of shared memory", tp->smem);
+    return -3;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kTrThreads, tp->smem) != cudaSuccess || per_sm < 1) {
+    set_last_error("trunk_plan: the trunk kernel does not fit on an SM");
+    return -3;
+  }
+  return 0;
+}
+
+int trunk_launch(const TrunkPlan& tp, cudaStream_t s) {
+  TrunkFn fn = trunk_kernel(tp.hd, tp.a.d);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tp.grid);
+  cfg.blockDim = dim3(kTrThreads);
+  cfg.dynamicSmemBytes = tp.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return (int)cudaLaunchKernelEx(&cfg, fn, tp.maps, tp.a);
+}
+
+}  // namespace cn

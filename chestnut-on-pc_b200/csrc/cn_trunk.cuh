@@ -1,0 +1,61 @@
+// Persistent transformer trunk (host interface).  See cn_trunk.cu.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cn {
+
+// GEMM slots of one layer, in execution order.
+enum TrunkGemm : int { TG_QKV = 0, TG_O = 1, TG_FC1 = 2, TG_FC2 = 3 };
+
+struct TrunkMaps {
+  CUtensorMap w[4];  // weights of all layers: [L][KB][N][64] f16, box 64 x 128
+  CUtensorMap x[4];  // GEMM inputs [M][K] f16, box 64 x ntok (rows >= M zero-filled)
+  CUtensorMap p[4];  // split-K partials [S][M][N] f32, box 128 x R x S
+  CUtensorMap r[4];  // residual rows of x [M][d] f32, box 128 x R (slots O and fc2)
+  CUtensorMap ps[4]; // the same partials as a store target, box 128 x M x 1
+};
+
+struct TrunkArgs {
+  int M;          // token rows (clips x tokens), <= 128
+  int ntok;       // MMA N: M rounded up to 16
+  int T, B;       // tokens per clip, clips
+  int d, mlp, heads, layers;
+  int N[4], K[4], S[4], units[4];  // per GEMM slot: features, reduction, split-K, CTAs with work
+  int R[4];                        // token rows per split-K reduction slice: ceil(M / S)
+  int stages, stage_bytes, x_bytes;
+  int aux_off, bar_off;            // shared-memory layout: ring at 0, then attention / reduction staging
+  int phases;                      // grid barriers per launch
+  float* x;                        // residual stream f32 [M][d]
+  __half *h, *qkv, *att, *u;       // LN out [M][d], qkv [M][3d], attention out [M][d], MLP hidden [M][mlp]
+  float* part;                     // split-K partials [S][M][N] (reused by every GEMM slot)
+  unsigned* tile_ctr;              // [layers][4][64] split-K arrival counters
+  unsigned long long* grid_ctr;    // grid barrier arrivals (monotonic)
+  unsigned* epoch;                 // completed launches
+  int* bump;                       // frame counter incremented once per launch (or null)
+  const float* bias[4];            // layer-0 biases; layer l at + l * bias_lstride
+  long long bias_lstride;
+};
+
+struct TrunkPlan {
+  TrunkMaps maps;
+  TrunkArgs a;
+  int grid;
+  size_t smem;
+  int hd;
+};
+
+// Scratch the trunk needs besides the activations: partial floats and the
+// counter block (zeroed once; cn_reset_state zeroes it again).
+size_t trunk_part_floats(int M, int d, int mlp, int layers, int nsm);
+size_t trunk_counter_bytes(int layers);
+bool trunk_supported(int M, int d, int heads);
+
+int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layers, const void* const w0[4],
+               long long w_lstride_bytes, const float* const b0[4], long long b_lstride, float* x, __half* h,
+               __half* qkv, __half* att, __half* u, float* part, void* counters, int* bump, int nsm);
+int trunk_launch(const TrunkPlan& tp, cudaStream_t s);
+
+}  // namespace cn

@@ -39,10 +39,15 @@ def params39():
     return omodel.gen_params(spec.CONFIGS["39m"], 3)
 
 
-def test_39m_frames_match_oracle_with_hidden_carry(params39):
+@pytest.mark.parametrize("trunk", ["persistent", "per-layer"])
+def test_39m_frames_match_oracle_with_hidden_carry(params39, trunk, monkeypatch):
+    # single-clip engines run the transformer as one persistent kernel unless CN_TRUNK=0
+    monkeypatch.setenv("CN_TRUNK", "1" if trunk == "persistent" else "0")
     rs = np.random.default_rng(0)
     w, pk = frame_inputs(rs, 12)
     eng = Engine("39m", seed=3)
+    names = [k["name"] for k in eng.kernel_list()]
+    assert ("transformer_trunk" in names) == (trunk == "persistent")
     clip = omodel.Clip("39m", 3, params39)
     pg, po = pk[0].copy(), pk[0].copy()
     for f in range(len(w)):
@@ -122,13 +127,33 @@ def test_batched_clips_match_single_clip_engines():
             assert all(ok for _, ok in errs.values()), (f, b, errs)
 
 
-def test_kernel_list_describes_the_frame():
+def test_kernel_list_describes_the_frame(monkeypatch):
+    # stem 10 + cond/tokens 3 + heads 3 GEMMs, the transformer as one persistent launch
     eng = Engine("39m", seed=0)
     ks = eng.kernel_list()
     names = [k["name"] for k in ks]
     assert names[0] == "queue_push" and names[1] == "border_gather0"
-    assert sum(n.startswith("gemm_tc") for n in names) == 10 + 3 + 4 * 4 + 3
+    assert sum(n.startswith("gemm_tc") for n in names) == 10 + 3 + 3
+    assert names.count("transformer_trunk") == 1
     assert eng.info()["n_kernels"] == len(ks)
+    # per-layer kernels: 4 GEMMs per layer
+    monkeypatch.setenv("CN_TRUNK", "0")
+    names = [k["name"] for k in Engine("39m", seed=0).kernel_list()]
+    assert sum(n.startswith("gemm_tc") for n in names) == 10 + 3 + 4 * 4 + 3
+    assert "transformer_trunk" not in names
+
+
+def test_persistent_trunk_is_deterministic_and_matches_per_layer_kernels(monkeypatch):
+    rs = np.random.default_rng(8)
+    w, pk = frame_inputs(rs, 4)
+    a, b = Engine("39m", seed=5), Engine("39m", seed=5, use_graph=False)
+    monkeypatch.setenv("CN_TRUNK", "0")
+    ref = Engine("39m", seed=5)
+    for f in range(4):
+        oa, ob, orf = a.run_frame(w[f], pk[f]), b.run_frame(w[f], pk[f]), ref.run_frame(w[f], pk[f])
+        assert np.array_equal(oa, ob), f          # graph replay == eager, run to run identical
+        errs = head_errors(oa, orf)
+        assert all(ok for _, ok in errs.values()), (f, errs)
 
 
 @pytest.mark.slow
