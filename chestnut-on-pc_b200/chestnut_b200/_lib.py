@@ -62,6 +62,7 @@ _SIGS = {
     "cn_param_info": ([_i, _i, ctypes.c_char_p, _i, ctypes.POINTER(_i), ctypes.POINTER(_ll), ctypes.POINTER(_ll),
                        ctypes.POINTER(_ll), ctypes.POINTER(_i)], _i),
     "cn_gemm_wmma_f16": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp], _i),
+    "cn_gemm_wmma_f16_noalloc": ([_vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
     "cn_reduce_rows_f16": ([_vp, _vp, _vp, _ll, _ll, _i, _vp], _i),
     "cn_border_gather_s2": ([_vp, _i, _i, _i, _i, _i, _vp, _vp], _i),
     "cn_device_error": ([ctypes.POINTER(_i)], _i),

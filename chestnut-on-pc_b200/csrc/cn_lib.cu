@@ -1,6 +1,7 @@
 // Single translation unit of libchestnut.so: device globals (the device error
 // word) are then shared by every kernel without relocatable device code.
 #include "cn_gemm.cu"
+#include "cn_gemm_noalloc.cu"
 #include "cn_reduce.cu"
 #include "cn_ops.cu"
 #include "cn_attn.cu"

@@ -122,6 +122,19 @@ int cn_param_info(int model, int index, char* name, int name_len, int* tensor_id
  * the same buffers cost one launch. */
 int cn_gemm_wmma_f16(const void* A, const void* B, float* C, int M, int N, int K, int b_kmajor, int bn,
                      int splits, void* stream);
+/* Same result as cn_gemm_wmma_f16 with b_kmajor = 1 (B is [N][K]), for callers
+ * that cannot allocate device memory (a host whose GPU memory belongs to
+ * another allocator, or a path where an allocation's implicit device
+ * synchronisation is not allowed).  No counterpart in the reference.  The
+ * split-K partial tiles and tile counters live in a 16 MiB static device array
+ * that every GPU loading the library holds until exit; calls needing more
+ * (splits x M x N rounded up to 128, x 4 bytes, plus 4 KiB of counters) or more
+ * than 1024 output tiles are rejected with CN_ERR_ARG.  splits in [1, 16] and
+ * <= ceil(K/64).  The first call on a device looks up the array's device
+ * address, so make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race. */
+int cn_gemm_wmma_f16_noalloc(const void* A, const void* B, float* C, int M, int N, int K, int splits,
+                             void* stream);
 /* out[r] = sum_i x[r][i] * w[i]; x f16 [rows][len], w f16 [len]; f32 out.
  * chunks_per_row in {1,2,4,8} (0 = automatic). */
 int cn_reduce_rows_f16(const void* x, const void* w, float* out, long long rows, long long len, int chunks_per_row,
