@@ -961,9 +961,14 @@ int cn_gemm_wmma_f16(const void* A, const void* B, float* C, int M, int N, int K
     ep.epi = EPI_F32_ACCUM;
     ep.out = C;
     ep.ldo = N;
+    ep.b_dep = 1;  // a caller's B may come from the previous kernel on the stream
     const bool mn = !b_kmajor;
     int r = gemm_plan(&g, A, K, 0, B, mn ? N : K, 0, M, N, K, 1, mn ? B_MN_MAJOR : B_K_MAJOR, bn, splits, ep);
     if (r) return r < 0 ? r : CN_ERR_CUDA;
+    // Programmatic dependent launch: back-to-back calls on one stream overlap
+    // the next call's launch and set-up with this call's tail; every operand
+    // is read only after griddepcontrol.wait.
+    g.pdl = true;
     std::lock_guard<std::mutex> lk(mu);
     keys[next] = key;
     plans[next] = g;

@@ -212,8 +212,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_3d(sA + stage * kA_Bytes, &tmA, &full[stage], kb * 64, m_tile * 128, group);
     };
     // B (weights) never depends on an earlier kernel: fill the first stages
-    // with it before waiting for the producer of A.
+    // with it before waiting for the producer of A (unless the caller says B
+    // may be produced by an earlier kernel).
     const int pre = nkb < ST ? nkb : ST;
+    if (p.b_dep) pdl_wait();
     for (int i = 0; i < pre; ++i) {
       mbar_arrive_expect_tx(&full[i], TL::Stage);
       load_b(i, kb0 + i);
@@ -304,8 +306,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async_smem();
     __syncthreads();
     if (S > 1) {
-      if (threadIdx.x == 0) {
-        for (int q = 0; q < S; ++q) {
+      // one slice per peer; a thread's bulk copies complete one after
+      // another, so the four warps share them
+      if (lane == 0) {
+        for (int q = warp; q < S; q += kThreads / 32) {
           if (q == split) continue;
           const int rq = owner_row0(q + 1, S) - owner_row0(q, S);
           bulk_s2cluster(map_shared_rank(smem_u32(rcv + split * rpo * LdC), (uint32_t)q),
@@ -314,6 +318,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       mbar_wait(recv_bar, (uint32_t)(ch & 1), 6);
+      // After the last chunk every copy into this CTA has landed: announce it
+      // now and wait for the others only before exiting (a CTA's staging tile
+      // is the source of its peers' copies).
+      if (ch + 1 == NCH) cluster_arrive();
     }
     if (xs && rows > 0) mbar_wait(xbar, (uint32_t)(ch & 1), 7);
     pdl_wait();  // the epilogue reads / writes activations of earlier kernels
@@ -330,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   // Peers' bulk copies out of this CTA's staging tile have landed once every
   // CTA of the cluster has received its last chunk.
-  if (S > 1) cluster_sync();
+  if (S > 1) cluster_wait();
 
   // Error path: do not leave a TMA write in flight into freed shared memory.
   if (warp == 0 && lane == 0 && g_cn_dev_error != 0) {

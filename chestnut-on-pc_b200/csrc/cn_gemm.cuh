@@ -39,6 +39,7 @@ struct GemmParams {
   const float* cond;  // [clips][cond_ld]
   long long cond_ld;
   int rows_per_clip, tok_base, tok_gstride, T;
+  int b_dep;          // 1: B may be written by an earlier kernel, so it is loaded only after griddepcontrol.wait
 };
 
 struct GemmPlan {
