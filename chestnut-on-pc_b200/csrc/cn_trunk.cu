@@ -47,6 +47,8 @@ constexpr int kTrThreads = 256;
 constexpr int kComputeThreads = 192;       // warps 2..7
 constexpr int kComputeT0 = 64;             // first compute thread
 constexpr int kWTileBytes = 128 * 64 * 2;  // one k-block of 128 output features
+constexpr int kKbPerStage = 2;              // k-blocks per ring stage (one TMA box each for W and X)
+constexpr int kWStageBytes = kKbPerStage * kWTileBytes;
 constexpr int kBarCompute = 1, kBarEpi = 2;
 constexpr int kPhasesPerLayer = 7;
 constexpr int kMaxTrunkSplit = 16;
@@ -154,18 +156,35 @@ __device__ __forceinline__ void store_out(const TrunkArgs& a, int gi, int t, int
   }
 }
 
-// Same for features n..n+3 (n % 4 == 0); old = the residual rows (O, fc2).
-__device__ __forceinline__ void store_out4(const TrunkArgs& a, int gi, int t, int n, float4 v, float4 old) {
-  const size_t i = (size_t)t * a.N[gi] + n;
-  if (gi == TG_QKV || gi == TG_FC1) {
-    const bool g = gi == TG_FC1;
-    __align__(8) __half hv[4] = {__float2half_rn(g ? apply_act(v.x, ACT_GELU) : v.x),
-                                 __float2half_rn(g ? apply_act(v.y, ACT_GELU) : v.y),
-                                 __float2half_rn(g ? apply_act(v.z, ACT_GELU) : v.z),
-                                 __float2half_rn(g ? apply_act(v.w, ACT_GELU) : v.w)};
-    *reinterpret_cast<uint2*>((g ? a.u : a.qkv) + i) = *reinterpret_cast<const uint2*>(hv);
-  } else {
-    *reinterpret_cast<float4*>(a.x + i) = make_float4(old.x + v.x, old.y + v.y, old.z + v.z, old.w + v.w);
+
+// Split-K reduction of tokens [t0, t1) of feature tile nt: the S slices
+// (S x R rows of 128 features, split order 0..S-1) and, for the residual slots,
+// the old x rows sit in shared memory; the slot's epilogue is compiled in.
+template <int GI>
+__device__ __forceinline__ void trunk_reduce(const TrunkArgs& a, const float* sl, const float* xres,
+                                             const float* bias, int S, int R, int t0, int t1, int nt, int ct) {
+  for (int i = ct; i < (t1 - t0) * 32; i += kComputeThreads) {
+    const int tt = i >> 5, fq = i & 31;
+    const float* row = sl + tt * 128 + 4 * fq;
+    float4 acc = *reinterpret_cast<const float4*>(row);
+    for (int q = 1; q < S; ++q) {
+      const float4 v = *reinterpret_cast<const float4*>(row + (size_t)q * R * 128);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    const float4 b4 = *reinterpret_cast<const float4*>(bias + 4 * fq);
+    acc.x += b4.x; acc.y += b4.y; acc.z += b4.z; acc.w += b4.w;
+    const size_t o = (size_t)(t0 + tt) * a.N[GI] + nt * 128 + 4 * fq;
+    if constexpr (GI == TG_O || GI == TG_FC2) {
+      const float4 old = *reinterpret_cast<const float4*>(xres + tt * 128 + 4 * fq);
+      *reinterpret_cast<float4*>(a.x + o) = make_float4(old.x + acc.x, old.y + acc.y, old.z + acc.z, old.w + acc.w);
+    } else {
+      const bool g = GI == TG_FC1;
+      __align__(8) __half hv[4] = {__float2half_rn(g ? apply_act(acc.x, ACT_GELU) : acc.x),
+                                   __float2half_rn(g ? apply_act(acc.y, ACT_GELU) : acc.y),
+                                   __float2half_rn(g ? apply_act(acc.z, ACT_GELU) : acc.z),
+                                   __float2half_rn(g ? apply_act(acc.w, ACT_GELU) : acc.w)};
+      *reinterpret_cast<uint2*>((g ? a.u : a.qkv) + o) = *reinterpret_cast<const uint2*>(hv);
+    }
   }
 }
 
@@ -395,11 +414,13 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               if ((int)blockIdx.x >= a.units[g2]) continue;
               int nt2, s2, k0, k1;
               unit_range(a, g2, blockIdx.x, &nt2, &s2, &k0, &k1);
-              for (int kb = k0; kb < k1; ++kb) tma_prefetch_l2_4d(&maps.w[g2], 0, nt2 * 128, kb, l2);
+              for (int kb = k0; kb < k1; kb += kKbPerStage) tma_prefetch_l2_4d(&maps.w[g2], 0, nt2 * 128, kb, l2);
               break;
             }
           }
-          for (int kb = kb0; kb < kb1; ++kb, ++g) {
+          // one stage = k-blocks kb, kb+1 (a box past the unit's range loads
+          // the neighbour's k-block, or zeros past K; the MMA skips it)
+          for (int kb = kb0; kb < kb1; kb += kKbPerStage, ++g) {
             if ((int)(g & 1) != warp) continue;
             const int st = (int)(g % ST);
             const uint32_t ph = (g / ST) & 1;
@@ -407,7 +428,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&fullW[st], kWTileBytes);
+            mbar_arrive_expect_tx(&fullW[st], kWStageBytes);
             tma_load_4d(smem + st * a.stage_bytes, &maps.w[gi], &fullW[st], 0, nt * 128, kb, l);
             last = g + 1;
           }
@@ -461,18 +482,18 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             const int t0 = s * M / S, t1 = (s + 1) * M / S;
             const bool resid = S > 1 && (gi == TG_O || gi == TG_FC2);
             // residual rows [t0, t0 + R) of this tile sit after the staging / slice rows
-            uint8_t* xres = aux + (size_t)(M > S * R ? M : S * R) * 512;
+            uint8_t* xres = aux + (size_t)(a.ntok > S * R ? a.ntok : S * R) * 512;
             if (warp == 2 || warp == 3) {
               // activation k-blocks: warp 2 the even ones, warp 3 the odd ones
               if (lane == 0) {
                 fence_proxy_async_global();
-                for (int i = 0; i < nkb; ++i, ++gx) {
+                for (int i = 0; i < nkb; i += kKbPerStage, ++gx) {
                   if ((int)(gx & 1) != warp - 2) continue;
                   const int st = (int)(gx % ST);
                   const uint32_t par = (gx / ST) & 1;
                   if (!mbar_wait(&empty[st], par ^ 1, 12)) break;
-                  mbar_arrive_expect_tx(&fullX[st], (uint32_t)a.x_bytes);
-                  tma_load_2d(smem + st * a.stage_bytes + kWTileBytes, &maps.x[gi], &fullX[st], (kb0 + i) * 64, 0);
+                  mbar_arrive_expect_tx(&fullX[st], (uint32_t)(kKbPerStage * a.x_bytes));
+                  tma_load_3d(smem + st * a.stage_bytes + kWStageBytes, &maps.x[gi], &fullX[st], 0, 0, kb0 + i);
                   x_last = gx + 1;
                 }
               }
@@ -488,17 +509,19 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             if (warp == 4 && lane == 0) {
               tc_fence_after();
               const uint32_t idesc = umma_idesc_f16(a.ntok, false);
-              for (int i = 0; i < nkb; ++i, ++gm) {
+              for (int i = 0; i < nkb; i += kKbPerStage, ++gm) {
                 const int st = (int)(gm % ST);
                 const uint32_t par = (gm / ST) & 1;
                 if (!mbar_wait(&fullW[st], par, 13) || !mbar_wait(&fullX[st], par, 1)) break;
                 tc_fence_after();
                 const uint32_t wa = smem_u32(smem + st * a.stage_bytes);
-                const uint32_t xa = wa + kWTileBytes;
+                const uint32_t xa = wa + kWStageBytes;
+                for (int h = 0; h < kKbPerStage && i + h < nkb; ++h)
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                  tc_mma_f16(tmem, umma_desc_sw128(wa + k * 32, 16, 1024), umma_desc_sw128(xa + k * 32, 16, 1024),
-                             idesc, (i > 0 || k > 0) ? 1u : 0u);
+                  for (int k = 0; k < 4; ++k)
+                    tc_mma_f16(tmem, umma_desc_sw128(wa + h * kWTileBytes + k * 32, 16, 1024),
+                               umma_desc_sw128(xa + h * a.x_bytes + k * 32, 16, 1024), idesc,
+                               (i > 0 || h > 0 || k > 0) ? 1u : 0u);
                 tc_commit(&empty[st]);
               }
               tc_commit(done);
@@ -527,20 +550,29 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                 // this feature tile meet on an arrival counter; unit s then
                 // reduces tokens [t0, t1) from one TMA box holding all S
                 // partials (split order 0..S-1) on the whole compute group.
+                // All ntok rows are staged (rows >= M are never stored: the TMA
+                // box stops at M).  Per-element row predicates here cost ~7x.
                 float* stg = reinterpret_cast<float*>(aux);
-                if (have)
-                  for (int c0 = 0; c0 < a.ntok; c0 += 64) {
-                    uint32_t r[4][16];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                      if (c0 + 16 * q < a.ntok) tmem_ld16(taddr + c0 + 16 * q, r[q]);
+                if (have) {
+                  int c0 = 0;
+                  for (; c0 + 32 <= a.ntok; c0 += 32) {
+                    uint32_t r[2][16];
+                    tmem_ld16(taddr + c0, r[0]);
+                    tmem_ld16(taddr + c0 + 16, r[1]);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
+                    for (int q = 0; q < 2; ++q)
 #pragma unroll
-                      for (int j = 0; j < 16; ++j)
-                        if (c0 + 16 * q + j < M) stg[(c0 + 16 * q + j) * 128 + e] = __uint_as_float(r[q][j]);
+                      for (int j = 0; j < 16; ++j) stg[(c0 + 16 * q + j) * 128 + e] = __uint_as_float(r[q][j]);
                   }
+                  if (c0 < a.ntok) {
+                    uint32_t r[16];
+                    tmem_ld16(taddr + c0, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) stg[(c0 + j) * 128 + e] = __uint_as_float(r[j]);
+                  }
+                }
                 tc_fence_before();
                 fence_proxy_async_smem();
                 named_sync(kBarEpi, 128);
@@ -578,20 +610,13 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               }
               if (landed) {
                 const float* bias = a.bias[gi] + (size_t)l * a.bias_lstride + nt * 128;
-                for (int i = ct; i < (t1 - t0) * 32; i += kComputeThreads) {
-                  const int tt = i >> 5, fq = i & 31;
-                  const float* row = reinterpret_cast<const float*>(aux) + tt * 128 + 4 * fq;
-                  float4 acc = *reinterpret_cast<const float4*>(row);
-                  for (int q = 1; q < S; ++q) {
-                    const float4 v = *reinterpret_cast<const float4*>(row + (size_t)q * R * 128);
-                    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-                  }
-                  const float4 b4 = *reinterpret_cast<const float4*>(bias + 4 * fq);
-                  acc.x += b4.x; acc.y += b4.y; acc.z += b4.z; acc.w += b4.w;
-                  const float4 old = resid ? *reinterpret_cast<const float4*>(
-                                                 reinterpret_cast<const float*>(xres) + tt * 128 + 4 * fq)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-                  store_out4(a, gi, t0 + tt, nt * 128 + 4 * fq, acc, old);
+                const float* sl = reinterpret_cast<const float*>(aux);
+                const float* xr = reinterpret_cast<const float*>(xres);
+                switch (gi) {
+                  case TG_QKV: trunk_reduce<TG_QKV>(a, sl, xr, bias, S, R, t0, t1, nt, ct); break;
+                  case TG_O: trunk_reduce<TG_O>(a, sl, xr, bias, S, R, t0, t1, nt, ct); break;
+                  case TG_FC1: trunk_reduce<TG_FC1>(a, sl, xr, bias, S, R, t0, t1, nt, ct); break;
+                  default: trunk_reduce<TG_FC2>(a, sl, xr, bias, S, R, t0, t1, nt, ct); break;
                 }
               }
               // the staging area is reused only after the grid barrier
@@ -685,13 +710,13 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
   }
   a.bias_lstride = b_lstride;
   a.x_bytes = a.ntok * 128;
-  a.stage_bytes = kWTileBytes + a.x_bytes;  // both multiples of 1 KB (SW128 atoms)
+  a.stage_bytes = kWStageBytes + kKbPerStage * a.x_bytes;  // all sub-tiles multiples of 1 KB (SW128 atoms)
   tp->hd = d / heads;
   // aux: attention staging, or the S reduction slices (+ residual rows) of a unit
   // aux: attention staging, or (staging tile | S reduction slices) + residual rows
   size_t aux_bytes = attn16_smem_bytes(tp->hd);
   for (int g = 0; g < 4; ++g) {
-    const size_t rows = (size_t)std::max(M, a.S[g] * a.R[g]) + ((g == TG_O || g == TG_FC2) ? a.R[g] : 0);
+    const size_t rows = (size_t)std::max(a.ntok, a.S[g] * a.R[g]) + ((g == TG_O || g == TG_FC2) ? a.R[g] : 0);
     aux_bytes = std::max(aux_bytes, rows * 512);
   }
   const size_t budget = 227 * 1024 - 1024 - 256;
@@ -726,17 +751,18 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
   for (int g = 0; g < 4; ++g) {
     const uint64_t dims[4] = {64, (uint64_t)N[g], (uint64_t)(K[g] / 64), (uint64_t)layers};
     const uint64_t strides[3] = {128, (uint64_t)N[g] * 128, (uint64_t)w_lstride_bytes};
-    const uint32_t box[4] = {64, 128, 1, 1};
+    const uint32_t box[4] = {64, 128, (uint32_t)kKbPerStage, 1};
     if (encode(&tp->maps.w[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, w0[g], dims, strides, box,
                CU_TENSOR_MAP_SWIZZLE_128B))
       return -3;
   }
   const __half* xin[4] = {h, att, h, u};
   for (int g = 0; g < 4; ++g) {
-    const uint64_t dims[2] = {(uint64_t)K[g], (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)K[g] * 2};
-    const uint32_t box[2] = {64, (uint32_t)a.ntok};
-    if (encode(&tp->maps.x[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xin[g], dims, strides, box,
+    // [M][K] viewed as (64-wide k, row, k-block): one box = kKbPerStage k-block tiles of ntok rows
+    const uint64_t dims[3] = {64, (uint64_t)M, (uint64_t)(K[g] / 64)};
+    const uint64_t strides[2] = {(uint64_t)K[g] * 2, 128};
+    const uint32_t box[3] = {64, (uint32_t)a.ntok, (uint32_t)kKbPerStage};
+    if (encode(&tp->maps.x[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, xin[g], dims, strides, box,
                CU_TENSOR_MAP_SWIZZLE_128B))
       return -3;
   }

@@ -11,8 +11,8 @@ namespace cn {
 enum TrunkGemm : int { TG_QKV = 0, TG_O = 1, TG_FC1 = 2, TG_FC2 = 3 };
 
 struct TrunkMaps {
-  CUtensorMap w[4];  // weights of all layers: [L][KB][N][64] f16, box 64 x 128
-  CUtensorMap x[4];  // GEMM inputs [M][K] f16, box 64 x ntok (rows >= M zero-filled)
+  CUtensorMap w[4];  // weights of all layers: [L][KB][N][64] f16, box 64 x 128 x 2 k-blocks
+  CUtensorMap x[4];  // GEMM inputs [M][K] f16 as (64, M, K/64), box 64 x ntok x 2 (rows >= M zero-filled)
   CUtensorMap p[4];  // split-K partials [S][M][N] f32, box 128 x R x S
   CUtensorMap r[4];  // residual rows of x [M][d] f32, box 128 x R (slots O and fc2)
   CUtensorMap ps[4]; // the same partials as a store target, box 128 x M x 1
