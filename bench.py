@@ -92,6 +92,18 @@ def frame_inputs(rng, n, batch):
     return w, pk
 
 
+def ncu_traffic(model):
+    """DRAM bytes (read + write) per trunk launch from the committed ncu capture
+    (profiles/trunk_1b_ncu.json, made with the command in profiles/trunk_1b.md)."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "trunk_%s_ncu.json" % model)
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d["dram_bytes_read"] + d["dram_bytes_write"]
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def trunk_bytes(d, mlp, rows, layers):
     """Algorithmic HBM bytes of one trunk launch: every layer's f16 weights and
     f32 biases, read once.  The activations of a single clip (88 token rows,
@@ -252,7 +264,7 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"kernel": kname, "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": src, "algorithmic_bytes_per_launch": kbytes, "avg_launch_ms": k_avg,
-                     "traffic": None},
+                     "traffic": ncu_traffic(args.model) if trunk else None},
         "frame_roofline": {"bound": "hbm", "weight_bytes": info["weight_bytes"],
                            "floor_ms": info["weight_bytes"] / (hbm * 1e9) * 1e3,
                            "frac": (info["weight_bytes"] / (hbm * 1e9) * 1e3) / lat[len(lat) // 2]},
