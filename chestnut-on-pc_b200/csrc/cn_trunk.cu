@@ -86,18 +86,12 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// Prefetch one weight tile (4-D k-blocked map) into L2; no completion tracking.
-__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
-  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-               : "memory");
-}
 // Shared -> global tiled store (no multicast), tracked by the bulk async-group.
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit_and_wait() {
@@ -403,21 +397,6 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           if ((int)blockIdx.x >= a.units[gi]) continue;
           int nt, s, kb0, kb1;
           unit_range(a, gi, blockIdx.x, &nt, &s, &kb0, &kb1);
-          if (warp == 0) {
-            // L2 look-ahead: request this CTA's next unit from HBM now.
-            for (int l2 = l, g2 = gi + 1; l2 < a.layers; ++g2) {
-              if (g2 == 4) {
-                g2 = -1;
-                ++l2;
-                continue;
-              }
-              if ((int)blockIdx.x >= a.units[g2]) continue;
-              int nt2, s2, k0, k1;
-              unit_range(a, g2, blockIdx.x, &nt2, &s2, &k0, &k1);
-              for (int kb = k0; kb < k1; kb += kKbPerStage) tma_prefetch_l2_4d(&maps.w[g2], 0, nt2 * 128, kb, l2);
-              break;
-            }
-          }
           // one stage = k-blocks kb, kb+1 (a box past the unit's range loads
           // the neighbour's k-block, or zeros past K; the MMA skips it)
           for (int kb = kb0; kb < kb1; kb += kKbPerStage, ++g) {
@@ -578,7 +557,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                 named_sync(kBarEpi, 128);
                 if (e == 0) {
                   if (have) {
-                    tma_store_3d(&maps.ps[gi], stg, nt * 128, 0, s);
+                    tma_store_4d(&maps.ps[gi], stg, 0, 0, nt, s);
                     bulk_commit_and_wait();  // written, and the staging tile is free again
                   }
                   fence_proxy_async_global();
@@ -591,7 +570,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                   flags[1] = met && have;
                   if (met && have) {
                     mbar_arrive_expect_tx(fixb, (uint32_t)(S * R) * 512u);
-                    tma_load_3d(aux, &maps.p[gi], fixb, nt * 128, t0, 0);
+                    tma_load_4d(aux, &maps.p[gi], fixb, 0, t0, nt, 0);
                   }
                 }
               }
@@ -767,14 +746,16 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
       return -3;
   }
   for (int g = 0; g < 4; ++g) {
-    const uint64_t dims[3] = {(uint64_t)N[g], (uint64_t)M, (uint64_t)a.S[g]};
-    const uint64_t strides[2] = {(uint64_t)N[g] * 4, (uint64_t)M * N[g] * 4};
-    const uint32_t box[3] = {128, (uint32_t)a.R[g], (uint32_t)a.S[g]};  // all S slices in one load
-    if (encode(&tp->maps.p[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, part, dims, strides, box,
+    // partials [S][N/128][M][128]: every unit's tile is one contiguous block
+    // (row-strided [S][M][N] tiles stored ~3.5x slower for N = 6144)
+    const uint64_t dims[4] = {128, (uint64_t)M, (uint64_t)(N[g] / 128), (uint64_t)a.S[g]};
+    const uint64_t strides[3] = {512, (uint64_t)M * 512, (uint64_t)M * N[g] * 4};
+    const uint32_t box[4] = {128, (uint32_t)a.R[g], 1, (uint32_t)a.S[g]};  // all S slices in one load
+    if (encode(&tp->maps.p[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part, dims, strides, box,
                CU_TENSOR_MAP_SWIZZLE_NONE))
       return -3;
-    const uint32_t sbox[3] = {128, (uint32_t)M, 1};
-    if (encode(&tp->maps.ps[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, part, dims, strides, sbox,
+    const uint32_t sbox[4] = {128, (uint32_t)M, 1, 1};
+    if (encode(&tp->maps.ps[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part, dims, strides, sbox,
                CU_TENSOR_MAP_SWIZZLE_NONE))
       return -3;
     const uint64_t xd[2] = {(uint64_t)d, (uint64_t)M};

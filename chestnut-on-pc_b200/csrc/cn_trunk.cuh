@@ -13,9 +13,9 @@ enum TrunkGemm : int { TG_QKV = 0, TG_O = 1, TG_FC1 = 2, TG_FC2 = 3 };
 struct TrunkMaps {
   CUtensorMap w[4];  // weights of all layers: [L][KB][N][64] f16, box 64 x 128 x 2 k-blocks
   CUtensorMap x[4];  // GEMM inputs [M][K] f16 as (64, M, K/64), box 64 x ntok x 2 (rows >= M zero-filled)
-  CUtensorMap p[4];  // split-K partials [S][M][N] f32, box 128 x R x S
+  CUtensorMap p[4];  // split-K partials [S][N/128][M][128] f32, box 128 x R x 1 x S
   CUtensorMap r[4];  // residual rows of x [M][d] f32, box 128 x R (slots O and fc2)
-  CUtensorMap ps[4]; // the same partials as a store target, box 128 x M x 1
+  CUtensorMap ps[4]; // the same partials as a store target, box 128 x M x 1 x 1
 };
 
 struct TrunkArgs {
@@ -30,7 +30,7 @@ struct TrunkArgs {
   int phases;                      // grid barriers per launch
   float* x;                        // residual stream f32 [M][d]
   __half *h, *qkv, *att, *u;       // LN out [M][d], qkv [M][3d], attention out [M][d], MLP hidden [M][mlp]
-  float* part;                     // split-K partials [S][M][N] (reused by every GEMM slot)
+  float* part;                     // split-K partials [S][N/128][M][128] (reused by every GEMM slot)
   unsigned* tile_ctr;              // [layers][4][64] split-K arrival counters
   unsigned long long* grid_ctr;    // grid barrier arrivals (monotonic)
   unsigned* epoch;                 // completed launches
