@@ -560,9 +560,9 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                     tma_store_4d(&maps.ps[gi], stg, 0, 0, nt, s);
                     bulk_commit_and_wait();  // written, and the staging tile is free again
                   }
-                  fence_proxy_async_global();
+                  // wait_group made the store's writes visible to this thread; the
+                  // release add publishes them (readers fence their TMA loads)
                   unsigned* ctr = a.tile_ctr + ((size_t)l * 4 + gi) * kMaxTiles + nt;
-                  fence_acq_rel_gpu();
                   red_release_add(ctr, 1u);
                   const bool met = spin_until(ctr, (unsigned)S * (epoch + 1u), 11, ld_acquire_u32);
                   fence_acq_rel_gpu();
