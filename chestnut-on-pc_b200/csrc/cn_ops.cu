@@ -121,7 +121,20 @@ __global__ void __launch_bounds__(128) k_gather0(Rings r, const float* __restric
     const uint4* src = reinterpret_cast<const uint4*>(row);
 #pragma unroll
     for (int q = 0; q < kK0Pad / 8; ++q) dst[q] = src[q];
-  } else if ((int)blockIdx.x < B) {
+  } else {
+    // features_buffer = feat_q[::4] after the push -> rows 0, 4, ..., 92, spread
+    // over every block of this grid row (one block alone took ~40 us)
+    const int nthr = gridDim.x * blockDim.x, tid = blockIdx.x * blockDim.x + threadIdx.x;
+    constexpr int kRow4 = kFeat / 4;
+    for (int i = tid; i < B * kNTemp * kRow4; i += nthr) {
+      const int b = i / (kNTemp * kRow4), j = (i / kRow4) % kNTemp, k4 = i % kRow4;
+      const float4 v = *reinterpret_cast<const float4*>(
+          r.feat + ((size_t)b * kFeatQ + (c + 1 + kFS * j) % kFeatQ) * kFeat + 4 * k4);
+      __align__(8) __half h[4] = {__float2half_rn(v.x), __float2half_rn(v.y), __float2half_rn(v.z),
+                                  __float2half_rn(v.w)};
+      *reinterpret_cast<uint2*>(feat16 + ((size_t)b * kNTemp + j) * kFeat + 4 * k4) = *reinterpret_cast<uint2*>(h);
+    }
+    if ((int)blockIdx.x >= B) return;
     const int b = blockIdx.x;
     const float* pk = packed + (size_t)b * kPacked;
     // cond = desire_pulse (25x8, max over FS groups of the 100-row queue) | tc | action_t | zero pad
@@ -138,12 +151,6 @@ __global__ void __launch_bounds__(128) k_gather0(Rings r, const float* __restric
         v = pk[kDesire + (i - kNDesire * kDesire)];  // traffic_convention then action_t
       }
       cond16[(size_t)b * kCondPad + i] = __float2half_rn(v);
-    }
-    // features_buffer = feat_q[::4] after the push -> rows 0, 4, ..., 92
-    for (int i = threadIdx.x; i < kNTemp * kFeat; i += blockDim.x) {
-      const int j = i / kFeat, k = i % kFeat;
-      const float v = r.feat[((size_t)b * kFeatQ + (c + 1 + kFS * j) % kFeatQ) * kFeat + k];
-      feat16[((size_t)b * kNTemp + j) * kFeat + k] = __float2half_rn(v);
     }
   }
 }
