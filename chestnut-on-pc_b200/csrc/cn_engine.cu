@@ -152,6 +152,7 @@ struct cn_engine {
   int nsm = 0;
   TrunkPlan trunk;
   float* part = nullptr;
+  __half* h2 = nullptr;  // LN2 output of the persistent trunk
   uint8_t* tctr = nullptr;
   size_t tctr_bytes = 0;
   std::vector<Step> steps;
@@ -273,6 +274,7 @@ static int layout_acts(cn_engine* e) {
   want((void**)&e->out, (size_t)B * kNOut * 4);
   if (e->use_trunk) {
     want((void**)&e->part, trunk_part_floats((int)R, m.d, m.mlp, m.layers, e->nsm) * 4);
+    want((void**)&e->h2, R * m.d * 2);
     e->tctr_bytes = trunk_counter_bytes(m.layers);
     want((void**)&e->tctr, e->tctr_bytes);
   }
@@ -454,7 +456,7 @@ static int build_plan(cn_engine* e) {
         }
       }
     CN_TRY(trunk_plan(&e->trunk, B, kT, m.d, m.mlp, m.heads, m.layers, w0, wstride, b0, bstride, e->x, e->h, e->qkv,
-                      e->att, e->u, e->part, e->tctr, e->rings.ctr, e->nsm));
+                      e->att, e->u, e->h2, e->part, e->tctr, e->rings.ctr, e->nsm));
     e->steps.push_back({"trunk", [e](cudaStream_t s) { return trunk_launch(e->trunk, s); },
                         kinfo("transformer_trunk", dim3(e->trunk.grid), dim3(256), dim3(1, 1, 1), e->trunk.smem)});
   }

@@ -53,6 +53,17 @@ constexpr int kBarCompute = 1, kBarEpi = 2;
 constexpr int kPhasesPerLayer = 7;
 constexpr int kMaxTrunkSplit = 16;
 constexpr int kMaxTiles = 64;  // feature tiles per GEMM slot (N <= 8192)
+// Dataflow counters of one layer (u32, monotonic across launches; a step is
+// complete for launch e once its counter reaches (e + 1) x contributions):
+constexpr int kDepPerLayer = 256;
+constexpr int kDepLn1 = 0;    // LN1 rows done (M per launch)
+constexpr int kDepLn2 = 1;    // LN2 rows done (M)
+constexpr int kDepO = 16;     // [slice] O reductions of token slice s done (N_O / 128 tiles)
+constexpr int kDepFc2 = 32;   // [slice] fc2 reductions of token slice s done (N_fc2 / 128)
+constexpr int kDepQkv = 64;   // [tile] QKV feature tile reduced (S_QKV units)
+constexpr int kDepAtt = 128;  // [head] attention rows of a head done (clips x 16-row blocks)
+constexpr int kDepFc1 = 192;  // [tile] fc1 feature tile reduced (S_fc1 units)
+constexpr int kBarRegion = 512;  // barriers, flags, LayerNorm partials
 
 __device__ __forceinline__ void named_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -127,6 +138,14 @@ __device__ __forceinline__ bool grid_sync(unsigned long long* ctr, unsigned long
   }
   named_sync(kBarCompute, kComputeThreads);
   return *flag != 0;
+}
+
+// Token slice of split s is [s*M/S, (s+1)*M/S); the slice that holds row r.
+__device__ __forceinline__ int slice_of(int M, int S, int r) {
+  int s = (int)(((long long)r * S) / M);
+  while (s > 0 && s * M / S > r) --s;
+  while (s + 1 < S && (s + 1) * M / S <= r) ++s;
+  return s;
 }
 
 __device__ __forceinline__ void unit_range(const TrunkArgs& a, int gi, int u, int* nt, int* s, int* kb0, int* kb1) {
@@ -421,24 +440,63 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------ compute group (warps 2..7)
+    // Dataflow instead of phase barriers: every step waits only for the
+    // counters of the data it reads (see the dependency table in dep_*), and
+    // publishes its own completion with a release add.  A CTA runs its steps
+    // in layer order, and each wait targets steps of earlier order, so the
+    // waits cannot form a cycle.
     const int ct = threadIdx.x - kComputeT0;
+    const unsigned ep1 = epoch + 1u;
     uint32_t gx = 0, gm = 0, ndone = 0, nfix = 0, nres = 0, x_last = 0;
-    unsigned long long bar_idx = (unsigned long long)epoch * a.phases;
-    const unsigned long long nb = gridDim.x;
     bool ok = true;
+    const int QB = (a.T + 15) / 16;
+    const int att_units = a.B * a.heads * QB;
     for (int l = 0; l < a.layers && ok; ++l) {
+      unsigned* dep = a.dep + (size_t)l * kDepPerLayer;
       for (int ph = 0; ph < kPhasesPerLayer && ok; ++ph) {
         if (ph == 0 || ph == 4) {
-          // ---------------- LayerNorm (x -> h), warps 4..7, one row at a time
+          // ---------------- LayerNorm (x -> h / h2), warps 4..7, one row at a time
+          const bool first = ph == 0;
           if (warp >= 4)
-            for (int r = blockIdx.x; r < a.M; r += gridDim.x)
-              ln_row<NV>(a.x, a.h, r, true, warp & 3, lane, lnpart, [] { named_sync(kBarEpi, 128); });
+            for (int r = blockIdx.x; r < a.M; r += gridDim.x) {
+              // row r is final once every feature tile of its token slice is
+              if (threadIdx.x == 128) {
+                bool met = true;
+                if (first && l > 0) {
+                  unsigned* pd = a.dep + (size_t)(l - 1) * kDepPerLayer;
+                  met = spin_until(pd + kDepFc2 + slice_of(a.M, a.S[TG_FC2], r), (unsigned)(a.N[TG_FC2] / 128) * ep1,
+                                   18, ld_acquire_u32);
+                } else if (!first) {
+                  met = spin_until(dep + kDepO + slice_of(a.M, a.S[TG_O], r), (unsigned)(a.N[TG_O] / 128) * ep1, 18,
+                                   ld_acquire_u32);
+                }
+                flags[2] = met;
+              }
+              named_sync(kBarEpi, 128);
+              const bool live = flags[2] != 0;  // (an expired wait has set the device error)
+              ln_row<NV>(a.x, first ? a.h : a.h2, r, live, warp & 3, lane, lnpart, [] { named_sync(kBarEpi, 128); });
+              fence_proxy_async_global();  // the rows are read by TMA
+              named_sync(kBarEpi, 128);
+              if (threadIdx.x == 128) {
+                fence_acq_rel_gpu();
+                red_release_add(dep + (first ? kDepLn1 : kDepLn2), 1u);
+              }
+            }
         } else if (ph == 2) {
           // ---------------- attention, one (clip, head, 16 query rows) per CTA
-          const int QB = (a.T + 15) / 16;
-          const int units = a.B * a.heads * QB;
-          for (int uu = blockIdx.x; uu < units; uu += gridDim.x) {
+          for (int uu = blockIdx.x; uu < att_units; uu += gridDim.x) {
             const int qb = uu % QB, h = (uu / QB) % a.heads, b = uu / (QB * a.heads);
+            if (threadIdx.x == kComputeT0) {
+              // q, k and v of head h (a 128-feature QKV tile holds 128 / HD heads)
+              const unsigned tgt = (unsigned)a.S[TG_QKV] * ep1;
+              bool met = spin_until(dep + kDepQkv + (h * HD) / 128, tgt, 19, ld_acquire_u32);
+              met = met && spin_until(dep + kDepQkv + (a.d + h * HD) / 128, tgt, 19, ld_acquire_u32);
+              met = met && spin_until(dep + kDepQkv + (2 * a.d + h * HD) / 128, tgt, 19, ld_acquire_u32);
+              fence_acq_rel_gpu();
+              flags[2] = met;
+            }
+            named_sync(kBarCompute, kComputeThreads);
+            if (flags[2] == 0) break;  // uniform: read after the barrier
             attn16_stage<HD>(a.qkv, attn, a.T, a.d, b, h, 16 * qb, ct, kComputeThreads);
             cp_async_wait_all();
             named_sync(kBarCompute, kComputeThreads);
@@ -448,7 +506,12 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               named_sync(kBarCompute, kComputeThreads);  // pairs with the one inside attn16_keys
             named_sync(kBarCompute, kComputeThreads);
             attn16_combine<HD>(attn, a.att, a.T, a.d, b, h, 16 * qb, ct, kComputeThreads);
+            fence_proxy_async_global();  // the attention rows are read by TMA
             named_sync(kBarCompute, kComputeThreads);
+            if (threadIdx.x == kComputeT0) {
+              fence_acq_rel_gpu();
+              red_release_add(dep + kDepAtt + h, 1u);
+            }
           }
         } else {
           // ---------------- GEMM slot
@@ -463,10 +526,24 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             // residual rows [t0, t0 + R) of this tile sit after the staging / slice rows
             uint8_t* xres = aux + (size_t)(a.ntok > S * R ? a.ntok : S * R) * 512;
             if (warp == 2 || warp == 3) {
-              // activation k-blocks: warp 2 the even ones, warp 3 the odd ones
+              // activation k-blocks: warp 2 the even ones, warp 3 the odd ones,
+              // once the producers of those k-blocks are done
               if (lane == 0) {
+                bool met = true;
+                if (gi == TG_QKV || gi == TG_FC1) {
+                  met = spin_until(dep + (gi == TG_QKV ? kDepLn1 : kDepLn2), (unsigned)M * ep1, 20, ld_acquire_u32);
+                } else {
+                  const int c0 = kb0 * 64, c1 = min(kb1 * 64, a.K[gi]) - 1;
+                  if (gi == TG_O) {
+                    for (int h = c0 / HD; h <= c1 / HD && met; ++h)
+                      met = spin_until(dep + kDepAtt + h, (unsigned)att_units / a.heads * ep1, 20, ld_acquire_u32);
+                  } else {
+                    for (int t = c0 / 128; t <= c1 / 128 && met; ++t)
+                      met = spin_until(dep + kDepFc1 + t, (unsigned)a.S[TG_FC1] * ep1, 20, ld_acquire_u32);
+                  }
+                }
                 fence_proxy_async_global();
-                for (int i = 0; i < nkb; i += kKbPerStage, ++gx) {
+                for (int i = 0; i < nkb && met; i += kKbPerStage, ++gx) {
                   if ((int)(gx & 1) != warp - 2) continue;
                   const int st = (int)(gx % ST);
                   const uint32_t par = (gx / ST) & 1;
@@ -479,9 +556,15 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               __syncwarp();
             } else if (warp == 5 && resid) {
               if (lane == 0) {
+                // x is final for this layer's O once every LN1 row is done, and
+                // for its fc2 once every LN2 row is
+                const bool met = spin_until(dep + (gi == TG_O ? kDepLn1 : kDepLn2), (unsigned)M * ep1, 21,
+                                            ld_acquire_u32);
                 fence_proxy_async_global();
-                mbar_arrive_expect_tx(rbar, (uint32_t)R * 512u);
-                tma_load_2d(xres, &maps.r[gi], rbar, nt * 128, t0);
+                if (met) {
+                  mbar_arrive_expect_tx(rbar, (uint32_t)R * 512u);
+                  tma_load_2d(xres, &maps.r[gi], rbar, nt * 128, t0);
+                }
               }
               __syncwarp();
             }
@@ -564,7 +647,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                   // release add publishes them (readers fence their TMA loads)
                   unsigned* ctr = a.tile_ctr + ((size_t)l * 4 + gi) * kMaxTiles + nt;
                   red_release_add(ctr, 1u);
-                  const bool met = spin_until(ctr, (unsigned)S * (epoch + 1u), 11, ld_acquire_u32);
+                  const bool met = spin_until(ctr, (unsigned)S * ep1, 11, ld_acquire_u32);
                   fence_acq_rel_gpu();
                   fence_proxy_async_global();
                   flags[1] = met && have;
@@ -575,9 +658,9 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                 }
               }
             }
+            // the whole compute group: reduce (split units), then publish
+            named_sync(kBarCompute, kComputeThreads);
             if (S > 1) {
-              // the whole compute group reduces once the slices have landed
-              named_sync(kBarCompute, kComputeThreads);
               bool landed = false;
               if (flags[1]) {
                 landed = mbar_wait(fixb, nfix & 1, 16);
@@ -598,14 +681,29 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                   default: trunk_reduce<TG_FC2>(a, sl, xr, bias, S, R, t0, t1, nt, ct); break;
                 }
               }
-              // the staging area is reused only after the grid barrier
+            }
+            fence_proxy_async_global();  // outputs read by TMA (h via LN, att, u) and cp.async
+            named_sync(kBarCompute, kComputeThreads);
+            if (threadIdx.x == kComputeT0) {
+              // tile nt (QKV, fc1) or token slice s (O, fc2) gained one unit
+              unsigned* c = dep + (gi == TG_QKV ? kDepQkv + nt
+                                                : gi == TG_FC1 ? kDepFc1 + nt : (gi == TG_O ? kDepO : kDepFc2) + s);
+              fence_acq_rel_gpu();
+              red_release_add(c, 1u);
             }
             ++ndone;
           }
         }
-        ok = grid_sync(a.grid_ctr, (++bar_idx) * nb, &flags[0]);
+        // one uniform verdict per step for the whole compute group (loops
+        // with named barriers must not diverge between warps)
+        named_sync(kBarCompute, kComputeThreads);
+        if (threadIdx.x == kComputeT0) flags[3] = !dev_error_set();
+        named_sync(kBarCompute, kComputeThreads);
+        ok = flags[3] != 0;
       }
     }
+    // one grid barrier per launch: every CTA has read the epoch before it moves on
+    if (!grid_sync(a.grid_ctr, (unsigned long long)ep1 * gridDim.x, &flags[0])) ok = false;
     if ((warp == 2 || warp == 3) && lane == 0 && !ok) {
       for (uint32_t i = x_last > (uint32_t)ST ? x_last - ST : 0; i < x_last; ++i)
         if ((int)(i & 1) == warp - 2) mbar_wait(&fullX[i % ST], (i / ST) & 1, 0, 100000000ull);
@@ -648,16 +746,18 @@ size_t trunk_part_floats(int M, int d, int mlp, int layers, int nsm) {
   size_t mx = 0;
   for (int g = 0; g < 4; ++g) {
     const size_t s = (size_t)trunk_split(N[g] / 128, K[g] / 64, nsm);
-    mx = std::max(mx, s * M * N[g]);
+    mx += s * M * N[g];  // one partial buffer per slot: steps of different slots overlap in time
   }
   return mx;
 }
 
-size_t trunk_counter_bytes(int layers) { return 256 + (size_t)layers * 4 * kMaxTiles * sizeof(unsigned); }
+size_t trunk_counter_bytes(int layers) {
+  return 256 + (size_t)layers * (4 * kMaxTiles + kDepPerLayer) * sizeof(unsigned);
+}
 
 int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layers, const void* const w0[4],
                long long w_lstride_bytes, const float* const b0[4], long long b_lstride, float* x, __half* h,
-               __half* qkv, __half* att, __half* u, float* part, void* counters, int* bump, int nsm) {
+               __half* qkv, __half* att, __half* u, __half* h2, float* part, void* counters, int* bump, int nsm) {
   const int M = B * T;
   if (!trunk_supported(M, d, heads) || T > 96 || (mlp % 128) || (d % 128) || mlp / 128 > kMaxTiles ||
       3 * d / 128 > kMaxTiles || (w_lstride_bytes % 16)) {
@@ -698,7 +798,7 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
     const size_t rows = (size_t)std::max(a.ntok, a.S[g] * a.R[g]) + ((g == TG_O || g == TG_FC2) ? a.R[g] : 0);
     aux_bytes = std::max(aux_bytes, rows * 512);
   }
-  const size_t budget = 227 * 1024 - 1024 - 256;
+  const size_t budget = 227 * 1024 - 1024 - kBarRegion;
   if (aux_bytes + 2 * (size_t)a.stage_bytes > budget) {
     set_last_error("trunk_plan: shared memory too small for the weight ring");
     return -2;
@@ -712,8 +812,8 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
   a.stages = st;
   a.aux_off = st * a.stage_bytes;
   a.bar_off = (int)((a.aux_off + aux_bytes + 63) / 64 * 64);
-  a.phases = kPhasesPerLayer * layers;
-  tp->smem = (size_t)a.bar_off + 256 + 1024;
+  a.phases = 1;  // grid barriers per launch (the closing one)
+  tp->smem = (size_t)a.bar_off + kBarRegion + 1024;
   a.x = x;
   a.h = h;
   a.qkv = qkv;
@@ -724,6 +824,8 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
   a.grid_ctr = reinterpret_cast<unsigned long long*>(c);
   a.epoch = reinterpret_cast<unsigned*>(c + 64);
   a.tile_ctr = reinterpret_cast<unsigned*>(c + 256);
+  a.dep = a.tile_ctr + (size_t)layers * 4 * kMaxTiles;
+  a.h2 = h2;
   a.bump = bump;
   tp->grid = nsm;
   // tensor maps
@@ -735,7 +837,7 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
                CU_TENSOR_MAP_SWIZZLE_128B))
       return -3;
   }
-  const __half* xin[4] = {h, att, h, u};
+  const __half* xin[4] = {h, att, h2, u};
   for (int g = 0; g < 4; ++g) {
     // [M][K] viewed as (64-wide k, row, k-block): one box = kKbPerStage k-block tiles of ntok rows
     const uint64_t dims[3] = {64, (uint64_t)M, (uint64_t)(K[g] / 64)};
@@ -745,17 +847,18 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
                CU_TENSOR_MAP_SWIZZLE_128B))
       return -3;
   }
+  float* part_g = part;
   for (int g = 0; g < 4; ++g) {
     // partials [S][N/128][M][128]: every unit's tile is one contiguous block
     // (row-strided [S][M][N] tiles stored ~3.5x slower for N = 6144)
     const uint64_t dims[4] = {128, (uint64_t)M, (uint64_t)(N[g] / 128), (uint64_t)a.S[g]};
     const uint64_t strides[3] = {512, (uint64_t)M * 512, (uint64_t)M * N[g] * 4};
     const uint32_t box[4] = {128, (uint32_t)a.R[g], 1, (uint32_t)a.S[g]};  // all S slices in one load
-    if (encode(&tp->maps.p[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part, dims, strides, box,
+    if (encode(&tp->maps.p[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part_g, dims, strides, box,
                CU_TENSOR_MAP_SWIZZLE_NONE))
       return -3;
     const uint32_t sbox[4] = {128, (uint32_t)M, 1, 1};
-    if (encode(&tp->maps.ps[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part, dims, strides, sbox,
+    if (encode(&tp->maps.ps[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part_g, dims, strides, sbox,
                CU_TENSOR_MAP_SWIZZLE_NONE))
       return -3;
     const uint64_t xd[2] = {(uint64_t)d, (uint64_t)M};
@@ -763,6 +866,7 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
     const uint32_t xb[2] = {128, (uint32_t)a.R[g]};
     if (encode(&tp->maps.r[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, x, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_NONE))
       return -3;
+    part_g += (size_t)a.S[g] * M * N[g];  // matches trunk_part_floats
   }
   TrunkFn fn = trunk_kernel(tp->hd, d);
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tp->smem) != cudaSuccess) {

@@ -27,11 +27,13 @@ struct TrunkArgs {
   int R[4];                        // token rows per split-K reduction slice: ceil(M / S)
   int stages, stage_bytes, x_bytes;
   int aux_off, bar_off;            // shared-memory layout: ring at 0, then attention / reduction staging
-  int phases;                      // grid barriers per launch
+  int phases;                      // grid barriers per launch (1: the closing one)
   float* x;                        // residual stream f32 [M][d]
-  __half *h, *qkv, *att, *u;       // LN out [M][d], qkv [M][3d], attention out [M][d], MLP hidden [M][mlp]
-  float* part;                     // split-K partials [S][N/128][M][128] (reused by every GEMM slot)
+  __half *h, *qkv, *att, *u;       // LN1 out [M][d], qkv [M][3d], attention out [M][d], MLP hidden [M][mlp]
+  __half* h2;                      // LN2 out [M][d] (its own buffer: LN2 rows overlap QKV steps still reading h)
+  float* part;                     // split-K partials, one [S][N/128][M][128] buffer per GEMM slot
   unsigned* tile_ctr;              // [layers][4][64] split-K arrival counters
+  unsigned* dep;                   // [layers][256] dataflow completion counters
   unsigned long long* grid_ctr;    // grid barrier arrivals (monotonic)
   unsigned* epoch;                 // completed launches
   int* bump;                       // frame counter incremented once per launch (or null)
@@ -55,7 +57,7 @@ bool trunk_supported(int M, int d, int heads);
 
 int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layers, const void* const w0[4],
                long long w_lstride_bytes, const float* const b0[4], long long b_lstride, float* x, __half* h,
-               __half* qkv, __half* att, __half* u, float* part, void* counters, int* bump, int nsm);
+               __half* qkv, __half* att, __half* u, __half* h2, float* part, void* counters, int* bump, int nsm);
 int trunk_launch(const TrunkPlan& tp, cudaStream_t s);
 
 }  // namespace cn
