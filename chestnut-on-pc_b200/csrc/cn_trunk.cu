@@ -6,19 +6,23 @@
 // pipeline fill and split-K epilogue before its successor can touch HBM.  This
 // kernel runs the whole trunk (layers x {LN1, QKV, attention, O + residual,
 // LN2, fc1 + GELU, fc2 + residual}) as one cooperative launch of one CTA per
-// SM, with a grid barrier between dependent phases, and decouples the weight
-// stream from the phases:
+// SM.  Steps meet on dataflow counters instead of grid barriers: a step waits
+// only for the counters of the rows / feature tiles it reads and publishes its
+// own completion with a release add.  The weight stream is decoupled from the
+// steps:
 //
-//   warp 0 (lane 0)  streams every weight k-block this CTA will consume, over
-//                    all layers, into a ring of shared-memory stages with TMA.
-//                    It waits only for free stages, never for phase barriers,
-//                    so HBM keeps streaming through barriers, LayerNorms and
-//                    attention.
-//   warps 1..7       the compute group.  In a GEMM phase warp 1 lane 0 loads
-//                    the activation k-blocks (TMA, after the barrier), warp 2
-//                    lane 0 issues tcgen05.mma and warps 4..7 run the
-//                    epilogue (TMEM lane quadrants 0..3).  LayerNorm uses
-//                    warps 4..7 (4 warps per row), attention warps 1..6.
+//   warps 0, 1 (lane 0)  stream every weight stage this CTA will consume, over
+//                        all layers, into a ring of shared-memory stages with
+//                        TMA (alternate stages per warp: a thread's loads
+//                        complete one after another).  They wait only for
+//                        free stages, never for the steps.
+//   warps 2..7           the compute group.  In a GEMM step warps 2 and 3
+//                        (lane 0) load the activation k-blocks once their
+//                        producers are done, warp 4 lane 0 issues tcgen05.mma,
+//                        warp 5 lane 0 loads residual rows and warps 4..7 run
+//                        the epilogue (TMEM lane quadrants 0..3); the split-K
+//                        reduction and attention use all six warps, LayerNorm
+//                        warps 4..7.
 //
 // GEMMs are computed transposed ("swap AB"): D[128 features][ntok tokens] =
 // W[128 x 64k] (A, the k-blocked weight tile) x X[ntok x 64k]^T (B), M = 128,
@@ -156,6 +160,50 @@ __device__ __forceinline__ void unit_range(const TrunkArgs& a, int gi, int u, in
   *kb1 = (*s + 1) * KB / S;
 }
 
+// Position in this CTA's weight stream: the stage starting at k-block kb of
+// its unit (layer l, slot gi, feature tile nt) whose k-blocks end at kb1.
+// The stream visits layers in order, slots 0..3, and each unit's k-blocks in
+// steps of kKbPerStage: the order in which the MMA issuer consumes stages.
+struct WPos {
+  int l, gi, nt, kb, kb1;
+};
+__device__ __forceinline__ void wpos_seek(const TrunkArgs& a, WPos& p) {
+  while (p.l < a.layers) {
+    if ((int)blockIdx.x < a.units[p.gi]) {
+      int s;
+      unit_range(a, p.gi, blockIdx.x, &p.nt, &s, &p.kb, &p.kb1);
+      return;
+    }
+    if (++p.gi == 4) {
+      p.gi = 0;
+      ++p.l;
+    }
+  }
+}
+__device__ __forceinline__ void wpos_next(const TrunkArgs& a, WPos& p) {
+  p.kb += kKbPerStage;
+  if (p.kb < p.kb1) return;
+  if (++p.gi == 4) {
+    p.gi = 0;
+    ++p.l;
+  }
+  wpos_seek(a, p);
+}
+
+// TMEM columns [c0, c0 + 16 * NL) of this warp's 32 lanes -> staging rows
+// [c0, c0 + 16 * NL) x 32 floats; all NL loads in flight before one wait.
+template <int NL>
+__device__ __forceinline__ void stage_cols(uint32_t taddr, int c0, float* stg, int lane) {
+  uint32_t r[NL][16];
+#pragma unroll
+  for (int q = 0; q < NL; ++q) tmem_ld16(taddr + c0 + 16 * q, r[q]);
+  tmem_ld_wait();
+#pragma unroll
+  for (int q = 0; q < NL; ++q)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) stg[(c0 + 16 * q + j) * 32 + lane] = __uint_as_float(r[q][j]);
+}
+
 // Final value of output (token t, feature n) of GEMM slot gi.
 __device__ __forceinline__ void store_out(const TrunkArgs& a, int gi, int t, int n, float v) {
   const size_t i = (size_t)t * a.N[gi] + n;
@@ -173,9 +221,12 @@ __device__ __forceinline__ void store_out(const TrunkArgs& a, int gi, int t, int
 // Split-K reduction of tokens [t0, t1) of feature tile nt: the S slices
 // (S x R rows of 128 features, split order 0..S-1) and, for the residual slots,
 // the old x rows sit in shared memory; the slot's epilogue is compiled in.
+// A thread always handles features 4 * (ct % 32) .. + 3 (the stride over
+// items is a multiple of 32), so its bias quad b4 is loaded once, early.
+static_assert(kComputeThreads % 32 == 0, "reduction items keep their feature quad");
 template <int GI>
-__device__ __forceinline__ void trunk_reduce(const TrunkArgs& a, const float* sl, const float* xres,
-                                             const float* bias, int S, int R, int t0, int t1, int nt, int ct) {
+__device__ __forceinline__ void trunk_reduce(const TrunkArgs& a, const float* sl, const float* xres, float4 b4,
+                                             int S, int R, int t0, int t1, int nt, int ct) {
   for (int i = ct; i < (t1 - t0) * 32; i += kComputeThreads) {
     const int tt = i >> 5, fq = i & 31;
     const float* row = sl + tt * 128 + 4 * fq;
@@ -184,7 +235,6 @@ __device__ __forceinline__ void trunk_reduce(const TrunkArgs& a, const float* sl
       const float4 v = *reinterpret_cast<const float4*>(row + (size_t)q * R * 128);
       acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
-    const float4 b4 = *reinterpret_cast<const float4*>(bias + 4 * fq);
     acc.x += b4.x; acc.y += b4.y; acc.z += b4.z; acc.w += b4.w;
     const size_t o = (size_t)(t0 + tt) * a.N[GI] + nt * 128 + 4 * fq;
     if constexpr (GI == TG_O || GI == TG_FC2) {
@@ -409,28 +459,24 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     // Two issuing warps (k-blocks alternate between them): a thread's TMA
     // loads complete one after another, so throughput scales with issuers.
     if (lane == 0) {
-      uint32_t g = 0, last = 0;
+      uint32_t last = 0;
       bool ok = true;
-      for (int l = 0; l < a.layers && ok; ++l)
-        for (int gi = 0; gi < 4 && ok; ++gi) {
-          if ((int)blockIdx.x >= a.units[gi]) continue;
-          int nt, s, kb0, kb1;
-          unit_range(a, gi, blockIdx.x, &nt, &s, &kb0, &kb1);
-          // one stage = k-blocks kb, kb+1 (a box past the unit's range loads
-          // the neighbour's k-block, or zeros past K; the MMA skips it)
-          for (int kb = kb0; kb < kb1; kb += kKbPerStage, ++g) {
-            if ((int)(g & 1) != warp) continue;
-            const int st = (int)(g % ST);
-            const uint32_t ph = (g / ST) & 1;
-            if (!mbar_wait(&empty[st], ph ^ 1, 14)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&fullW[st], kWStageBytes);
-            tma_load_4d(smem + st * a.stage_bytes, &maps.w[gi], &fullW[st], 0, nt * 128, kb, l);
-            last = g + 1;
-          }
+      WPos cur = {0, 0, 0, 0, 0};
+      wpos_seek(a, cur);
+      // one stage = k-blocks kb, kb+1 (a box past the unit's range loads
+      // the neighbour's k-block, or zeros past K; the MMA skips it)
+      for (uint32_t g = 0; cur.l < a.layers; ++g, wpos_next(a, cur)) {
+        if ((int)(g & 1) != warp) continue;
+        const int st = (int)(g % ST);
+        const uint32_t ph = (g / ST) & 1;
+        if (!mbar_wait(&empty[st], ph ^ 1, 14)) {
+          ok = false;
+          break;
         }
+        mbar_arrive_expect_tx(&fullW[st], kWStageBytes);
+        tma_load_4d(smem + st * a.stage_bytes, &maps.w[cur.gi], &fullW[st], 0, cur.nt * 128, cur.kb, cur.l);
+        last = g + 1;
+      }
       if (!ok || dev_error_set()) {
         // do not leave a TMA write in flight into shared memory of an exiting CTA
         for (uint32_t i = last > (uint32_t)ST ? last - ST : 0; i < last; ++i)
@@ -477,10 +523,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               ln_row<NV>(a.x, first ? a.h : a.h2, r, live, warp & 3, lane, lnpart, [] { named_sync(kBarEpi, 128); });
               fence_proxy_async_global();  // the rows are read by TMA
               named_sync(kBarEpi, 128);
-              if (threadIdx.x == 128) {
-                fence_acq_rel_gpu();
-                red_release_add(dep + (first ? kDepLn1 : kDepLn2), 1u);
-              }
+              if (threadIdx.x == 128) red_release_add(dep + (first ? kDepLn1 : kDepLn2), 1u);
             }
         } else if (ph == 2) {
           // ---------------- attention, one (clip, head, 16 query rows) per CTA
@@ -508,10 +551,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             attn16_combine<HD>(attn, a.att, a.T, a.d, b, h, 16 * qb, ct, kComputeThreads);
             fence_proxy_async_global();  // the attention rows are read by TMA
             named_sync(kBarCompute, kComputeThreads);
-            if (threadIdx.x == kComputeT0) {
-              fence_acq_rel_gpu();
-              red_release_add(dep + kDepAtt + h, 1u);
-            }
+            if (threadIdx.x == kComputeT0) red_release_add(dep + kDepAtt + h, 1u);
           }
         } else {
           // ---------------- GEMM slot
@@ -523,6 +563,11 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             const int S = a.S[gi], M = a.M, R = a.R[gi];
             const int t0 = s * M / S, t1 = (s + 1) * M / S;
             const bool resid = S > 1 && (gi == TG_O || gi == TG_FC2);
+            // bias quad of this thread's reduction features, in flight during the MMAs
+            float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (S > 1)
+              b4 = __ldg(reinterpret_cast<const float4*>(a.bias[gi] + (size_t)l * a.bias_lstride + nt * 128) +
+                         (ct & 31));
             // residual rows [t0, t0 + R) of this tile sit after the staging / slice rows
             uint8_t* xres = aux + (size_t)(a.ntok > S * R ? a.ntok : S * R) * 512;
             if (warp == 2 || warp == 3) {
@@ -608,43 +653,37 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                   }
                 tc_fence_before();
               } else {
-                // partial tile -> shared staging -> one TMA store; the S units of
+                // partial tile -> shared staging -> TMA stores; the S units of
                 // this feature tile meet on an arrival counter; unit s then
                 // reduces tokens [t0, t1) from one TMA box holding all S
                 // partials (split order 0..S-1) on the whole compute group.
-                // All ntok rows are staged (rows >= M are never stored: the TMA
-                // box stops at M).  Per-element row predicates here cost ~7x.
-                float* stg = reinterpret_cast<float*>(aux);
+                // Each epilogue warp stages its 32 features for all ntok rows
+                // ([row][32] floats) and stores them itself: TMA stores from
+                // four issuing threads run concurrently.  Rows >= M are staged
+                // but never stored (the box stops at M); per-element row
+                // predicates here cost ~7x.
+                float* stg = reinterpret_cast<float*>(aux) + (warp & 3) * a.ntok * 32;
                 if (have) {
                   int c0 = 0;
-                  for (; c0 + 32 <= a.ntok; c0 += 32) {
-                    uint32_t r[2][16];
-                    tmem_ld16(taddr + c0, r[0]);
-                    tmem_ld16(taddr + c0 + 16, r[1]);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int q = 0; q < 2; ++q)
-#pragma unroll
-                      for (int j = 0; j < 16; ++j) stg[(c0 + 16 * q + j) * 128 + e] = __uint_as_float(r[q][j]);
+                  for (; c0 + 64 <= a.ntok; c0 += 64) stage_cols<4>(taddr, c0, stg, lane);
+                  if (c0 + 32 <= a.ntok) {
+                    stage_cols<2>(taddr, c0, stg, lane);
+                    c0 += 32;
                   }
-                  if (c0 < a.ntok) {
-                    uint32_t r[16];
-                    tmem_ld16(taddr + c0, r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) stg[(c0 + j) * 128 + e] = __uint_as_float(r[j]);
-                  }
+                  if (c0 < a.ntok) stage_cols<1>(taddr, c0, stg, lane);
                 }
                 tc_fence_before();
                 fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && have) {
+                  tma_store_4d(&maps.ps[gi], stg, 32 * (warp & 3), 0, nt, s);
+                  bulk_commit_and_wait();  // written, and the staging rows are free again
+                }
                 named_sync(kBarEpi, 128);
                 if (e == 0) {
-                  if (have) {
-                    tma_store_4d(&maps.ps[gi], stg, 0, 0, nt, s);
-                    bulk_commit_and_wait();  // written, and the staging tile is free again
-                  }
-                  // wait_group made the store's writes visible to this thread; the
-                  // release add publishes them (readers fence their TMA loads)
+                  // each warp's wait_group made its store's writes visible to its
+                  // issuing thread, the barrier orders them before this release
+                  // (readers fence their TMA loads)
                   unsigned* ctr = a.tile_ctr + ((size_t)l * 4 + gi) * kMaxTiles + nt;
                   red_release_add(ctr, 1u);
                   const bool met = spin_until(ctr, (unsigned)S * ep1, 11, ld_acquire_u32);
@@ -671,14 +710,13 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                 ++nres;
               }
               if (landed) {
-                const float* bias = a.bias[gi] + (size_t)l * a.bias_lstride + nt * 128;
                 const float* sl = reinterpret_cast<const float*>(aux);
                 const float* xr = reinterpret_cast<const float*>(xres);
                 switch (gi) {
-                  case TG_QKV: trunk_reduce<TG_QKV>(a, sl, xr, bias, S, R, t0, t1, nt, ct); break;
-                  case TG_O: trunk_reduce<TG_O>(a, sl, xr, bias, S, R, t0, t1, nt, ct); break;
-                  case TG_FC1: trunk_reduce<TG_FC1>(a, sl, xr, bias, S, R, t0, t1, nt, ct); break;
-                  default: trunk_reduce<TG_FC2>(a, sl, xr, bias, S, R, t0, t1, nt, ct); break;
+                  case TG_QKV: trunk_reduce<TG_QKV>(a, sl, xr, b4, S, R, t0, t1, nt, ct); break;
+                  case TG_O: trunk_reduce<TG_O>(a, sl, xr, b4, S, R, t0, t1, nt, ct); break;
+                  case TG_FC1: trunk_reduce<TG_FC1>(a, sl, xr, b4, S, R, t0, t1, nt, ct); break;
+                  default: trunk_reduce<TG_FC2>(a, sl, xr, b4, S, R, t0, t1, nt, ct); break;
                 }
               }
             }
@@ -688,7 +726,6 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               // tile nt (QKV, fc1) or token slice s (O, fc2) gained one unit
               unsigned* c = dep + (gi == TG_QKV ? kDepQkv + nt
                                                 : gi == TG_FC1 ? kDepFc1 + nt : (gi == TG_O ? kDepO : kDepFc2) + s);
-              fence_acq_rel_gpu();
               red_release_add(c, 1u);
             }
             ++ndone;
@@ -857,7 +894,7 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
     if (encode(&tp->maps.p[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part_g, dims, strides, box,
                CU_TENSOR_MAP_SWIZZLE_NONE))
       return -3;
-    const uint32_t sbox[4] = {128, (uint32_t)M, 1, 1};
+    const uint32_t sbox[4] = {32, (uint32_t)M, 1, 1};  // one epilogue warp's 32 features
     if (encode(&tp->maps.ps[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part_g, dims, strides, sbox,
                CU_TENSOR_MAP_SWIZZLE_NONE))
       return -3;

@@ -15,7 +15,7 @@ struct TrunkMaps {
   CUtensorMap x[4];  // GEMM inputs [M][K] f16 as (64, M, K/64), box 64 x ntok x 2 (rows >= M zero-filled)
   CUtensorMap p[4];  // split-K partials [S][N/128][M][128] f32, box 128 x R x 1 x S
   CUtensorMap r[4];  // residual rows of x [M][d] f32, box 128 x R (slots O and fc2)
-  CUtensorMap ps[4]; // the same partials as a store target, box 128 x M x 1 x 1
+  CUtensorMap ps[4]; // the same partials as a store target, box 32 x M x 1 x 1 (one epilogue warp's features)
 };
 
 struct TrunkArgs {
