@@ -184,18 +184,15 @@ __global__ void k_gather_s2(const __half* __restrict__ act, int G, int B, int Hi
 // partial sums are combined in warp order, so the result is deterministic.
 // part[4][2] is shared scratch of the 4 warps and sync() synchronises them.
 // Rows with live == false take part in the synchronisation only.
+// ln_vals normalises a row whose values the warps already hold: v[i] are
+// features q * d / 4 + 4 * (lane + 32 * i) .. + 3 of the row.
 template <int NV, typename Sync>
-__device__ __forceinline__ void ln_row(const float* __restrict__ x, __half* __restrict__ y, int row, bool live, int q,
-                                       int lane, float (*part)[2], Sync sync) {
+__device__ __forceinline__ void ln_vals(const float4 (&v)[NV], __half* __restrict__ y, int row, bool live, int q,
+                                        int lane, float (*part)[2], Sync sync) {
   constexpr int d = NV * 512;
-  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(live ? row : 0) * d + q * (d / 4));
-  float4 v[NV];
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    v[i] = live ? __ldcg(xr + lane + 32 * i) : make_float4(0.f, 0.f, 0.f, 0.f);  // L2: rows written by other SMs
-    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-  }
+  for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if (lane == 0) part[q][0] = s;
@@ -224,6 +221,18 @@ __device__ __forceinline__ void ln_row(const float* __restrict__ x, __half* __re
     u.y = *reinterpret_cast<uint32_t*>(&h1);
     yr[lane + 32 * i] = u;
   }
+}
+
+template <int NV, typename Sync>
+__device__ __forceinline__ void ln_row(const float* __restrict__ x, __half* __restrict__ y, int row, bool live, int q,
+                                       int lane, float (*part)[2], Sync sync) {
+  constexpr int d = NV * 512;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(live ? row : 0) * d + q * (d / 4));
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+    v[i] = live ? __ldcg(xr + lane + 32 * i) : make_float4(0.f, 0.f, 0.f, 0.f);  // L2: rows written by other SMs
+  ln_vals<NV>(v, y, row, live, q, lane, part, sync);
 }
 
 // 2 rows per 256-thread block.

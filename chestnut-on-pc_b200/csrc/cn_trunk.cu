@@ -4,11 +4,11 @@
 // 88 tokens of activations, so it is an HBM stream with small dependent steps
 // in between.  Launched as separate kernels, every GEMM pays its launch,
 // pipeline fill and split-K epilogue before its successor can touch HBM.  This
-// kernel runs the whole trunk (layers x {LN1, QKV, attention, O + residual,
-// LN2, fc1 + GELU, fc2 + residual}) as one cooperative launch of one CTA per
-// SM.  Steps meet on dataflow counters instead of grid barriers: a step waits
-// only for the counters of the rows / feature tiles it reads and publishes its
-// own completion with a release add.  The weight stream is decoupled from the
+// kernel runs the whole trunk (layers x {LN1, QKV, attention, O, LN2, fc1 +
+// GELU, fc2}) as one cooperative launch of one CTA per SM.  Steps meet on
+// dataflow counters instead of grid barriers: a step waits only for the
+// counters of the rows / feature tiles it reads and publishes its own
+// completion with a release add.  The weight stream is decoupled from the
 // steps:
 //
 //   warps 0, 1 (lane 0)  stream every weight stage this CTA will consume, over
@@ -18,19 +18,23 @@
 //                        free stages, never for the steps.
 //   warps 2..7           the compute group.  In a GEMM step warps 2 and 3
 //                        (lane 0) load the activation k-blocks once their
-//                        producers are done, warp 4 lane 0 issues tcgen05.mma,
-//                        warp 5 lane 0 loads residual rows and warps 4..7 run
-//                        the epilogue (TMEM lane quadrants 0..3); the split-K
-//                        reduction and attention use all six warps, LayerNorm
-//                        warps 4..7.
+//                        producers are done, warp 4 lane 0 issues tcgen05.mma
+//                        and warps 4..7 run the epilogue (TMEM lane quadrants
+//                        0..3); the QKV / fc1 split-K reduction and attention
+//                        use all six warps, the row steps warps 4..7.
 //
 // GEMMs are computed transposed ("swap AB"): D[128 features][ntok tokens] =
 // W[128 x 64k] (A, the k-blocked weight tile) x X[ntok x 64k]^T (B), M = 128,
 // N = ntok (88 tokens -> 96), f32 accumulator in TMEM.  A GEMM slot is cut
-// into units (128-feature tile, split-K part); a unit with S > 1 writes its
-// partial tile to an L2-resident scratch, the S units of a feature tile meet
-// on an arrival counter, and unit s then reduces tokens [s*M/S, (s+1)*M/S) in
-// split order 0..S-1 (deterministic) and applies bias / GELU / residual.
+// into units (128-feature tile, split-K part); a unit writes its partial tile
+// to an L2-resident scratch.  QKV / fc1: the S units of a feature tile meet on
+// an arrival counter, and unit s then reduces tokens [s*M/S, (s+1)*M/S) in
+// split order 0..S-1 (deterministic) and applies bias / GELU, so that
+// attention and fc2 can start on single heads / tiles.  O / fc2 feed the
+// residual stream, whose next reader (LayerNorm) needs whole rows: there the
+// CTA of row r sums the row's partials in split order, adds bias and residual
+// and normalises in one row step, one hop instead of a reduction hop plus a
+// LayerNorm hop.
 //
 // Every wait is bounded (%globaltimer); on timeout a code lands in the device
 // error word and the kernel unwinds instead of hanging.  Counters are
@@ -62,12 +66,13 @@ constexpr int kMaxTiles = 64;  // feature tiles per GEMM slot (N <= 8192)
 constexpr int kDepPerLayer = 256;
 constexpr int kDepLn1 = 0;    // LN1 rows done (M per launch)
 constexpr int kDepLn2 = 1;    // LN2 rows done (M)
-constexpr int kDepO = 16;     // [slice] O reductions of token slice s done (N_O / 128 tiles)
-constexpr int kDepFc2 = 32;   // [slice] fc2 reductions of token slice s done (N_fc2 / 128)
+constexpr int kDepOp = 2;     // O units whose split-K partials are stored (units_O)
+constexpr int kDepFc2p = 3;   // fc2 units whose split-K partials are stored (units_fc2)
 constexpr int kDepQkv = 64;   // [tile] QKV feature tile reduced (S_QKV units)
 constexpr int kDepAtt = 128;  // [head] attention rows of a head done (clips x 16-row blocks)
 constexpr int kDepFc1 = 192;  // [tile] fc1 feature tile reduced (S_fc1 units)
 constexpr int kBarRegion = 512;  // barriers, flags, LayerNorm partials
+constexpr int kRowChunk = 5;     // split-K slices a row step loads per round trip
 
 __device__ __forceinline__ void named_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -144,14 +149,6 @@ __device__ __forceinline__ bool grid_sync(unsigned long long* ctr, unsigned long
   return *flag != 0;
 }
 
-// Token slice of split s is [s*M/S, (s+1)*M/S); the slice that holds row r.
-__device__ __forceinline__ int slice_of(int M, int S, int r) {
-  int s = (int)(((long long)r * S) / M);
-  while (s > 0 && s * M / S > r) --s;
-  while (s + 1 < S && (s + 1) * M / S <= r) ++s;
-  return s;
-}
-
 __device__ __forceinline__ void unit_range(const TrunkArgs& a, int gi, int u, int* nt, int* s, int* kb0, int* kb1) {
   const int S = a.S[gi], KB = a.K[gi] / 64;
   *nt = u / S;
@@ -204,29 +201,25 @@ __device__ __forceinline__ void stage_cols(uint32_t taddr, int c0, float* stg, i
     for (int j = 0; j < 16; ++j) stg[(c0 + 16 * q + j) * 32 + lane] = __uint_as_float(r[q][j]);
 }
 
-// Final value of output (token t, feature n) of GEMM slot gi.
+// Final value of output (token t, feature n) of GEMM slot QKV or fc1.
 __device__ __forceinline__ void store_out(const TrunkArgs& a, int gi, int t, int n, float v) {
   const size_t i = (size_t)t * a.N[gi] + n;
-  if (gi == TG_QKV) {
+  if (gi == TG_QKV)
     a.qkv[i] = __float2half_rn(v);
-  } else if (gi == TG_FC1) {
+  else
     a.u[i] = __float2half_rn(apply_act(v, ACT_GELU));
-  } else {
-    float* px = a.x + i;
-    *px = __ldcg(px) + v;
-  }
 }
 
 
-// Split-K reduction of tokens [t0, t1) of feature tile nt: the S slices
-// (S x R rows of 128 features, split order 0..S-1) and, for the residual slots,
-// the old x rows sit in shared memory; the slot's epilogue is compiled in.
+// Split-K reduction of tokens [t0, t1) of feature tile nt of slot QKV or fc1:
+// the S slices (S x R rows of 128 features, split order 0..S-1) sit in shared
+// memory; the slot's epilogue is compiled in.
 // A thread always handles features 4 * (ct % 32) .. + 3 (the stride over
 // items is a multiple of 32), so its bias quad b4 is loaded once, early.
 static_assert(kComputeThreads % 32 == 0, "reduction items keep their feature quad");
 template <int GI>
-__device__ __forceinline__ void trunk_reduce(const TrunkArgs& a, const float* sl, const float* xres, float4 b4,
-                                             int S, int R, int t0, int t1, int nt, int ct) {
+__device__ __forceinline__ void trunk_reduce(const TrunkArgs& a, const float* sl, float4 b4, int S, int R, int t0,
+                                             int t1, int nt, int ct) {
   for (int i = ct; i < (t1 - t0) * 32; i += kComputeThreads) {
     const int tt = i >> 5, fq = i & 31;
     const float* row = sl + tt * 128 + 4 * fq;
@@ -237,18 +230,79 @@ __device__ __forceinline__ void trunk_reduce(const TrunkArgs& a, const float* sl
     }
     acc.x += b4.x; acc.y += b4.y; acc.z += b4.z; acc.w += b4.w;
     const size_t o = (size_t)(t0 + tt) * a.N[GI] + nt * 128 + 4 * fq;
-    if constexpr (GI == TG_O || GI == TG_FC2) {
-      const float4 old = *reinterpret_cast<const float4*>(xres + tt * 128 + 4 * fq);
-      *reinterpret_cast<float4*>(a.x + o) = make_float4(old.x + acc.x, old.y + acc.y, old.z + acc.z, old.w + acc.w);
-    } else {
-      const bool g = GI == TG_FC1;
-      __align__(8) __half hv[4] = {__float2half_rn(g ? apply_act(acc.x, ACT_GELU) : acc.x),
-                                   __float2half_rn(g ? apply_act(acc.y, ACT_GELU) : acc.y),
-                                   __float2half_rn(g ? apply_act(acc.z, ACT_GELU) : acc.z),
-                                   __float2half_rn(g ? apply_act(acc.w, ACT_GELU) : acc.w)};
-      *reinterpret_cast<uint2*>((g ? a.u : a.qkv) + o) = *reinterpret_cast<const uint2*>(hv);
+    const bool g = GI == TG_FC1;
+    __align__(8) __half hv[4] = {__float2half_rn(g ? apply_act(acc.x, ACT_GELU) : acc.x),
+                                 __float2half_rn(g ? apply_act(acc.y, ACT_GELU) : acc.y),
+                                 __float2half_rn(g ? apply_act(acc.z, ACT_GELU) : acc.z),
+                                 __float2half_rn(g ? apply_act(acc.w, ACT_GELU) : acc.w)};
+    *reinterpret_cast<uint2*>((g ? a.u : a.qkv) + o) = *reinterpret_cast<const uint2*>(hv);
+  }
+}
+
+// Row step of the residual stream on warps 4..7 (named barrier kBarEpi), in
+// ln_row's feature layout: warp q holds features q * d / 4 + 4 * (lane + 32 i).
+// With a source slot (O or fc2 of layer sl) row r of x is first brought up to
+// date: the split-K partials of its feature tiles are added in split order
+// 0..S-1, then the bias, then the old row (the residual), and x is written
+// back.  The partials are waited for as a whole (src_done >= target): a row
+// needs every feature tile, and every tile every split.  With y the row is
+// then normalised into y.  Returns false if the wait expired.
+template <int NV>
+__device__ __forceinline__ bool trunk_row(const TrunkArgs& a, int src, int sl, const unsigned* src_done,
+                                          unsigned target, __half* y, int r, int q, int lane, volatile int* flags,
+                                          float (*lnpart)[2]) {
+  constexpr int d = NV * 512;
+  float* xr = a.x + (size_t)r * d + q * (d / 4) + 4 * lane;
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)  // x row r is written only by this CTA's row steps (same threads) or before the launch
+    v[i] = __ldcg(reinterpret_cast<const float4*>(xr + 128 * i));
+  bool live = true;
+  if (src >= 0) {
+    float4 b[NV];
+    const float* bias = a.bias[src] + (size_t)sl * a.bias_lstride + q * (d / 4) + 4 * lane;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) b[i] = __ldg(reinterpret_cast<const float4*>(bias + 128 * i));
+    if (threadIdx.x == 128) flags[2] = spin_until(src_done, target, 18, ld_acquire_u32);
+    named_sync(kBarEpi, 128);
+    live = flags[2] != 0;
+    if (live) {
+      // partials [S][d / 128][M][128]: feature tile of v[i] is q * NV + i, column 4 * lane
+      const size_t ss = (size_t)a.M * d, ts = (size_t)a.M * 128;
+      const float* p = a.pslot[src] + (size_t)r * 128 + 4 * lane + (size_t)q * NV * ts;
+      // kRowChunk slices per L2 round trip (a load-then-add loop over a runtime
+      // S serialises one round trip per slice); sums stay in split order
+      const int S = a.S[src];
+      float4 acc[NV];
+      for (int s0 = 0; s0 < S; s0 += kRowChunk) {
+        float4 t[kRowChunk][NV];
+#pragma unroll
+        for (int j = 0; j < kRowChunk; ++j)
+#pragma unroll
+          for (int i = 0; i < NV; ++i)
+            t[j][i] = s0 + j < S ? __ldcg(reinterpret_cast<const float4*>(p + (s0 + j) * ss + i * ts))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < kRowChunk; ++j)
+#pragma unroll
+          for (int i = 0; i < NV; ++i) {
+            if (s0 + j == 0) {
+              acc[i] = t[j][i];
+            } else if (s0 + j < S) {
+              acc[i].x += t[j][i].x; acc[i].y += t[j][i].y; acc[i].z += t[j][i].z; acc[i].w += t[j][i].w;
+            }
+          }
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        acc[i].x += b[i].x; acc[i].y += b[i].y; acc[i].z += b[i].z; acc[i].w += b[i].w;
+        v[i] = make_float4(v[i].x + acc[i].x, v[i].y + acc[i].y, v[i].z + acc[i].z, v[i].w + acc[i].w);
+        *reinterpret_cast<float4*>(xr + 128 * i) = v[i];
+      }
     }
   }
+  if (y) ln_vals<NV>(v, y, r, live, q, lane, lnpart, [] { named_sync(kBarEpi, 128); });
+  return live;
 }
 
 // Attention of query rows [q0, q0 + 16) of (clip b, head h).  Shared layout
@@ -419,7 +473,6 @@ __global__ void __launch_bounds__(kTrThreads, 1)
   uint64_t* empty = fullW + 16;
   uint64_t* done = fullW + 24;
   uint64_t* fixb = fullW + 25;  // reduction slices landed
-  uint64_t* rbar = fullW + 26;  // residual rows landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fullW + 27);
   volatile int* flags = reinterpret_cast<volatile int*>(fullW + 28);  // [0] grid barrier, [1] tile counter
   float(*lnpart)[2] = reinterpret_cast<float(*)[2]>(fullW + 30);     // 4 x 2 floats
@@ -435,7 +488,6 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     }
     mbar_init(done, 1);
     mbar_init(fixb, 1);
-    mbar_init(rbar, 1);
     fence_barrier_init();
     for (int g = 0; g < 4; ++g) {
       tma_prefetch_desc(&maps.w[g]);
@@ -493,7 +545,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     // waits cannot form a cycle.
     const int ct = threadIdx.x - kComputeT0;
     const unsigned ep1 = epoch + 1u;
-    uint32_t gx = 0, gm = 0, ndone = 0, nfix = 0, nres = 0, x_last = 0;
+    uint32_t gx = 0, gm = 0, ndone = 0, nfix = 0, x_last = 0;
     bool ok = true;
     const int QB = (a.T + 15) / 16;
     const int att_units = a.B * a.heads * QB;
@@ -501,27 +553,24 @@ __global__ void __launch_bounds__(kTrThreads, 1)
       unsigned* dep = a.dep + (size_t)l * kDepPerLayer;
       for (int ph = 0; ph < kPhasesPerLayer && ok; ++ph) {
         if (ph == 0 || ph == 4) {
-          // ---------------- LayerNorm (x -> h / h2), warps 4..7, one row at a time
+          // ---------------- row step (fc2 of layer l-1 / O of layer l -> x, LayerNorm -> h / h2),
+          // warps 4..7, one row at a time
           const bool first = ph == 0;
+          int src = -1, sl = l;
+          const unsigned* sd = dep + kDepOp;
+          unsigned tgt = (unsigned)a.units[TG_O] * ep1;
+          if (!first) {
+            src = TG_O;
+          } else if (l > 0) {
+            src = TG_FC2;
+            sl = l - 1;
+            sd = a.dep + (size_t)(l - 1) * kDepPerLayer + kDepFc2p;
+            tgt = (unsigned)a.units[TG_FC2] * ep1;
+          }
           if (warp >= 4)
             for (int r = blockIdx.x; r < a.M; r += gridDim.x) {
-              // row r is final once every feature tile of its token slice is
-              if (threadIdx.x == 128) {
-                bool met = true;
-                if (first && l > 0) {
-                  unsigned* pd = a.dep + (size_t)(l - 1) * kDepPerLayer;
-                  met = spin_until(pd + kDepFc2 + slice_of(a.M, a.S[TG_FC2], r), (unsigned)(a.N[TG_FC2] / 128) * ep1,
-                                   18, ld_acquire_u32);
-                } else if (!first) {
-                  met = spin_until(dep + kDepO + slice_of(a.M, a.S[TG_O], r), (unsigned)(a.N[TG_O] / 128) * ep1, 18,
-                                   ld_acquire_u32);
-                }
-                flags[2] = met;
-              }
-              named_sync(kBarEpi, 128);
-              const bool live = flags[2] != 0;  // (an expired wait has set the device error)
-              ln_row<NV>(a.x, first ? a.h : a.h2, r, live, warp & 3, lane, lnpart, [] { named_sync(kBarEpi, 128); });
-              fence_proxy_async_global();  // the rows are read by TMA
+              trunk_row<NV>(a, src, sl, sd, tgt, first ? a.h : a.h2, r, warp & 3, lane, flags, lnpart);
+              fence_proxy_async_global();  // the normalised rows are read by TMA
               named_sync(kBarEpi, 128);
               if (threadIdx.x == 128) red_release_add(dep + (first ? kDepLn1 : kDepLn2), 1u);
             }
@@ -562,53 +611,43 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             const int nkb = kb1 - kb0;
             const int S = a.S[gi], M = a.M, R = a.R[gi];
             const int t0 = s * M / S, t1 = (s + 1) * M / S;
-            const bool resid = S > 1 && (gi == TG_O || gi == TG_FC2);
+            // O and fc2 units only publish partials: the row steps reduce them
+            const bool rowred = gi == TG_O || gi == TG_FC2;
             // bias quad of this thread's reduction features, in flight during the MMAs
             float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (S > 1)
+            if (S > 1 && !rowred)
               b4 = __ldg(reinterpret_cast<const float4*>(a.bias[gi] + (size_t)l * a.bias_lstride + nt * 128) +
                          (ct & 31));
-            // residual rows [t0, t0 + R) of this tile sit after the staging / slice rows
-            uint8_t* xres = aux + (size_t)(a.ntok > S * R ? a.ntok : S * R) * 512;
             if (warp == 2 || warp == 3) {
-              // activation k-blocks: warp 2 the even ones, warp 3 the odd ones,
-              // once the producers of those k-blocks are done
+              // activation k-blocks: warp 2 the even stages, warp 3 the odd
+              // ones, each once the producers of its k-blocks are done: QKV /
+              // fc1 read every row of h / h2; an O stage reads the heads, an
+              // fc2 stage the fc1 feature tiles of its own k-blocks, so the
+              // MMAs start on the first ready stage
               if (lane == 0) {
                 bool met = true;
-                if (gi == TG_QKV || gi == TG_FC1) {
+                if (gi == TG_QKV || gi == TG_FC1)
                   met = spin_until(dep + (gi == TG_QKV ? kDepLn1 : kDepLn2), (unsigned)M * ep1, 20, ld_acquire_u32);
-                } else {
-                  const int c0 = kb0 * 64, c1 = min(kb1 * 64, a.K[gi]) - 1;
-                  if (gi == TG_O) {
-                    for (int h = c0 / HD; h <= c1 / HD && met; ++h)
-                      met = spin_until(dep + kDepAtt + h, (unsigned)att_units / a.heads * ep1, 20, ld_acquire_u32);
-                  } else {
-                    for (int t = c0 / 128; t <= c1 / 128 && met; ++t)
-                      met = spin_until(dep + kDepFc1 + t, (unsigned)a.S[TG_FC1] * ep1, 20, ld_acquire_u32);
-                  }
-                }
-                fence_proxy_async_global();
                 for (int i = 0; i < nkb && met; i += kKbPerStage, ++gx) {
                   if ((int)(gx & 1) != warp - 2) continue;
+                  if (gi == TG_O || gi == TG_FC2) {
+                    const int c0 = (kb0 + i) * 64, c1 = min(kb0 + i + kKbPerStage, kb1) * 64 - 1;
+                    if (gi == TG_O) {
+                      for (int h = c0 / HD; h <= c1 / HD && met; ++h)
+                        met = spin_until(dep + kDepAtt + h, (unsigned)att_units / a.heads * ep1, 20, ld_acquire_u32);
+                    } else {
+                      for (int t = c0 / 128; t <= c1 / 128 && met; ++t)
+                        met = spin_until(dep + kDepFc1 + t, (unsigned)a.S[TG_FC1] * ep1, 20, ld_acquire_u32);
+                    }
+                    if (!met) break;
+                  }
+                  fence_proxy_async_global();
                   const int st = (int)(gx % ST);
                   const uint32_t par = (gx / ST) & 1;
                   if (!mbar_wait(&empty[st], par ^ 1, 12)) break;
                   mbar_arrive_expect_tx(&fullX[st], (uint32_t)(kKbPerStage * a.x_bytes));
                   tma_load_3d(smem + st * a.stage_bytes + kWStageBytes, &maps.x[gi], &fullX[st], 0, 0, kb0 + i);
                   x_last = gx + 1;
-                }
-              }
-              __syncwarp();
-            } else if (warp == 5 && resid) {
-              if (lane == 0) {
-                // x is final for this layer's O once every LN1 row is done, and
-                // for its fc2 once every LN2 row is
-                const bool met = spin_until(dep + (gi == TG_O ? kDepLn1 : kDepLn2), (unsigned)M * ep1, 21,
-                                            ld_acquire_u32);
-                fence_proxy_async_global();
-                if (met) {
-                  mbar_arrive_expect_tx(rbar, (uint32_t)R * 512u);
-                  tma_load_2d(xres, &maps.r[gi], rbar, nt * 128, t0);
                 }
               }
               __syncwarp();
@@ -640,7 +679,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
               const bool have = mbar_wait(done, ndone & 1, 15);
               tc_fence_after();
-              if (S == 1) {
+              if (S == 1 && !rowred) {
                 const float bv = a.bias[gi][(size_t)l * a.bias_lstride + n];
                 if (have)
                   for (int c = 0; c < a.ntok; c += 16) {
@@ -653,11 +692,11 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                   }
                 tc_fence_before();
               } else {
-                // partial tile -> shared staging -> TMA stores; the S units of
-                // this feature tile meet on an arrival counter; unit s then
-                // reduces tokens [t0, t1) from one TMA box holding all S
-                // partials (split order 0..S-1) on the whole compute group.
-                // Each epilogue warp stages its 32 features for all ntok rows
+                // partial tile -> shared staging -> TMA stores.  QKV / fc1: the
+                // S units of this feature tile meet on an arrival counter; unit
+                // s then reduces tokens [t0, t1) from one TMA box holding all S
+                // partials (split order 0..S-1) on the whole compute group.  O /
+                // fc2: the unit is done; the row steps reduce.  Each epilogue warp stages its 32 features for all ntok rows
                 // ([row][32] floats) and stores them itself: TMA stores from
                 // four issuing threads run concurrently.  Rows >= M are staged
                 // but never stored (the box stops at M); per-element row
@@ -680,10 +719,12 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                   bulk_commit_and_wait();  // written, and the staging rows are free again
                 }
                 named_sync(kBarEpi, 128);
-                if (e == 0) {
-                  // each warp's wait_group made its store's writes visible to its
-                  // issuing thread, the barrier orders them before this release
-                  // (readers fence their TMA loads)
+                // each warp's wait_group made its store's writes visible to its
+                // issuing thread, the barrier orders them before the release add
+                // (TMA readers fence their loads)
+                if (rowred) {
+                  if (e == 0) red_release_add(dep + (gi == TG_O ? kDepOp : kDepFc2p), 1u);
+                } else if (e == 0) {
                   unsigned* ctr = a.tile_ctr + ((size_t)l * 4 + gi) * kMaxTiles + nt;
                   red_release_add(ctr, 1u);
                   const bool met = spin_until(ctr, (unsigned)S * ep1, 11, ld_acquire_u32);
@@ -699,34 +740,25 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             }
             // the whole compute group: reduce (split units), then publish
             named_sync(kBarCompute, kComputeThreads);
-            if (S > 1) {
-              bool landed = false;
-              if (flags[1]) {
-                landed = mbar_wait(fixb, nfix & 1, 16);
-                ++nfix;
-              }
-              if (resid) {
-                landed = mbar_wait(rbar, nres & 1, 17) && landed;
-                ++nres;
-              }
-              if (landed) {
-                const float* sl = reinterpret_cast<const float*>(aux);
-                const float* xr = reinterpret_cast<const float*>(xres);
-                switch (gi) {
-                  case TG_QKV: trunk_reduce<TG_QKV>(a, sl, xr, b4, S, R, t0, t1, nt, ct); break;
-                  case TG_O: trunk_reduce<TG_O>(a, sl, xr, b4, S, R, t0, t1, nt, ct); break;
-                  case TG_FC1: trunk_reduce<TG_FC1>(a, sl, xr, b4, S, R, t0, t1, nt, ct); break;
-                  default: trunk_reduce<TG_FC2>(a, sl, xr, b4, S, R, t0, t1, nt, ct); break;
+            if (!rowred) {
+              if (S > 1) {
+                bool landed = false;
+                if (flags[1]) {
+                  landed = mbar_wait(fixb, nfix & 1, 16);
+                  ++nfix;
+                }
+                if (landed) {
+                  const float* sl = reinterpret_cast<const float*>(aux);
+                  if (gi == TG_QKV)
+                    trunk_reduce<TG_QKV>(a, sl, b4, S, R, t0, t1, nt, ct);
+                  else
+                    trunk_reduce<TG_FC1>(a, sl, b4, S, R, t0, t1, nt, ct);
                 }
               }
-            }
-            fence_proxy_async_global();  // outputs read by TMA (h via LN, att, u) and cp.async
-            named_sync(kBarCompute, kComputeThreads);
-            if (threadIdx.x == kComputeT0) {
-              // tile nt (QKV, fc1) or token slice s (O, fc2) gained one unit
-              unsigned* c = dep + (gi == TG_QKV ? kDepQkv + nt
-                                                : gi == TG_FC1 ? kDepFc1 + nt : (gi == TG_O ? kDepO : kDepFc2) + s);
-              red_release_add(c, 1u);
+              fence_proxy_async_global();  // outputs read by cp.async (qkv, attention) and TMA (u, fc2)
+              named_sync(kBarCompute, kComputeThreads);
+              // feature tile nt gained one unit
+              if (threadIdx.x == kComputeT0) red_release_add(dep + (gi == TG_QKV ? kDepQkv : kDepFc1) + nt, 1u);
             }
             ++ndone;
           }
@@ -739,6 +771,11 @@ __global__ void __launch_bounds__(kTrThreads, 1)
         ok = flags[3] != 0;
       }
     }
+    // the last fc2 brought into x (no LayerNorm follows inside the trunk)
+    if (ok && warp >= 4)
+      for (int r = blockIdx.x; r < a.M; r += gridDim.x)
+        trunk_row<NV>(a, TG_FC2, a.layers - 1, a.dep + (size_t)(a.layers - 1) * kDepPerLayer + kDepFc2p,
+                      (unsigned)a.units[TG_FC2] * ep1, nullptr, r, warp & 3, lane, flags, lnpart);
     // one grid barrier per launch: every CTA has read the epoch before it moves on
     if (!grid_sync(a.grid_ctr, (unsigned long long)ep1 * gridDim.x, &flags[0])) ok = false;
     if ((warp == 2 || warp == 3) && lane == 0 && !ok) {
@@ -828,13 +865,10 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
   a.x_bytes = a.ntok * 128;
   a.stage_bytes = kWStageBytes + kKbPerStage * a.x_bytes;  // all sub-tiles multiples of 1 KB (SW128 atoms)
   tp->hd = d / heads;
-  // aux: attention staging, or the S reduction slices (+ residual rows) of a unit
-  // aux: attention staging, or (staging tile | S reduction slices) + residual rows
-  size_t aux_bytes = attn16_smem_bytes(tp->hd);
-  for (int g = 0; g < 4; ++g) {
-    const size_t rows = (size_t)std::max(a.ntok, a.S[g] * a.R[g]) + ((g == TG_O || g == TG_FC2) ? a.R[g] : 0);
-    aux_bytes = std::max(aux_bytes, rows * 512);
-  }
+  // aux: attention staging, or the partial staging tile (ntok rows) / the S
+  // reduction slices of a QKV or fc1 unit
+  size_t aux_bytes = std::max(attn16_smem_bytes(tp->hd), (size_t)a.ntok * 512);
+  for (int g : {TG_QKV, TG_FC1}) aux_bytes = std::max(aux_bytes, (size_t)a.S[g] * a.R[g] * 512);
   const size_t budget = 227 * 1024 - 1024 - kBarRegion;
   if (aux_bytes + 2 * (size_t)a.stage_bytes > budget) {
     set_last_error("trunk_plan: shared memory too small for the weight ring");
@@ -898,11 +932,7 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
     if (encode(&tp->maps.ps[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part_g, dims, strides, sbox,
                CU_TENSOR_MAP_SWIZZLE_NONE))
       return -3;
-    const uint64_t xd[2] = {(uint64_t)d, (uint64_t)M};
-    const uint64_t xs[1] = {(uint64_t)d * 4};
-    const uint32_t xb[2] = {128, (uint32_t)a.R[g]};
-    if (encode(&tp->maps.r[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, x, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return -3;
+    a.pslot[g] = part_g;
     part_g += (size_t)a.S[g] * M * N[g];  // matches trunk_part_floats
   }
   TrunkFn fn = trunk_kernel(tp->hd, d);

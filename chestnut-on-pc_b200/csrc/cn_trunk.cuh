@@ -14,7 +14,6 @@ struct TrunkMaps {
   CUtensorMap w[4];  // weights of all layers: [L][KB][N][64] f16, box 64 x 128 x 2 k-blocks
   CUtensorMap x[4];  // GEMM inputs [M][K] f16 as (64, M, K/64), box 64 x ntok x 2 (rows >= M zero-filled)
   CUtensorMap p[4];  // split-K partials [S][N/128][M][128] f32, box 128 x R x 1 x S
-  CUtensorMap r[4];  // residual rows of x [M][d] f32, box 128 x R (slots O and fc2)
   CUtensorMap ps[4]; // the same partials as a store target, box 32 x M x 1 x 1 (one epilogue warp's features)
 };
 
@@ -32,6 +31,7 @@ struct TrunkArgs {
   __half *h, *qkv, *att, *u;       // LN1 out [M][d], qkv [M][3d], attention out [M][d], MLP hidden [M][mlp]
   __half* h2;                      // LN2 out [M][d] (its own buffer: LN2 rows overlap QKV steps still reading h)
   float* part;                     // split-K partials, one [S][N/128][M][128] buffer per GEMM slot
+  float* pslot[4];                 // the buffer of each slot
   unsigned* tile_ctr;              // [layers][4][64] split-K arrival counters
   unsigned* dep;                   // [layers][256] dataflow completion counters
   unsigned long long* grid_ctr;    // grid barrier arrivals (monotonic)
