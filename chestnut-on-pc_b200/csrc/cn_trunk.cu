@@ -106,18 +106,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// Shared -> global tiled store (no multicast), tracked by the bulk async-group.
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2,
-                                             int c3) {
-  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit_and_wait() {
-  asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group 0;" ::: "memory");
-}
-
 // Spin until *ctr >= target (bounded).  false on timeout or a recorded error.
 template <typename T, typename Ld>
 __device__ __forceinline__ bool spin_until(const T* ctr, T target, int code, Ld ld) {
@@ -187,10 +175,12 @@ __device__ __forceinline__ void wpos_next(const TrunkArgs& a, WPos& p) {
   wpos_seek(a, p);
 }
 
-// TMEM columns [c0, c0 + 16 * NL) of this warp's 32 lanes -> staging rows
-// [c0, c0 + 16 * NL) x 32 floats; all NL loads in flight before one wait.
+// TMEM columns [c0, c0 + 16 * NL) of this warp's 32 lanes -> partial rows
+// [c0, c0 + 16 * NL) (rows >= M skipped), all NL loads in flight before one
+// wait.  Lane i of the warp owns one feature, so every store instruction
+// writes one whole 128-byte row segment of the tile-contiguous layout.
 template <int NL>
-__device__ __forceinline__ void stage_cols(uint32_t taddr, int c0, float* stg, int lane) {
+__device__ __forceinline__ void store_cols(uint32_t taddr, int c0, float* dst, int M) {
   uint32_t r[NL][16];
 #pragma unroll
   for (int q = 0; q < NL; ++q) tmem_ld16(taddr + c0 + 16 * q, r[q]);
@@ -198,7 +188,10 @@ __device__ __forceinline__ void stage_cols(uint32_t taddr, int c0, float* stg, i
 #pragma unroll
   for (int q = 0; q < NL; ++q)
 #pragma unroll
-    for (int j = 0; j < 16; ++j) stg[(c0 + 16 * q + j) * 32 + lane] = __uint_as_float(r[q][j]);
+    for (int j = 0; j < 16; ++j) {
+      const int t = c0 + 16 * q + j;
+      if (t < M) dst[(size_t)t * 128] = __uint_as_float(r[q][j]);
+    }
 }
 
 // Final value of output (token t, feature n) of GEMM slot QKV or fc1.
@@ -692,36 +685,28 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                   }
                 tc_fence_before();
               } else {
-                // partial tile -> shared staging -> TMA stores.  QKV / fc1: the
-                // S units of this feature tile meet on an arrival counter; unit
-                // s then reduces tokens [t0, t1) from one TMA box holding all S
-                // partials (split order 0..S-1) on the whole compute group.  O /
-                // fc2: the unit is done; the row steps reduce.  Each epilogue warp stages its 32 features for all ntok rows
-                // ([row][32] floats) and stores them itself: TMA stores from
-                // four issuing threads run concurrently.  Rows >= M are staged
-                // but never stored (the box stops at M); per-element row
-                // predicates here cost ~7x.
-                float* stg = reinterpret_cast<float*>(aux) + (warp & 3) * a.ntok * 32;
+                // partial tile -> global, straight from the TMEM registers
+                // (staging in shared memory and one TMA store per warp took
+                // ~0.5 us longer per unit).  QKV / fc1: the S units of this
+                // feature tile meet on an arrival counter; unit s then reduces
+                // tokens [t0, t1) from one TMA box holding all S partials
+                // (split order 0..S-1) on the whole compute group.  O / fc2:
+                // the unit is done; the row steps reduce.
+                float* dst = a.pslot[gi] + ((size_t)s * (a.N[gi] / 128) + nt) * (size_t)M * 128 + e;
                 if (have) {
                   int c0 = 0;
-                  for (; c0 + 64 <= a.ntok; c0 += 64) stage_cols<4>(taddr, c0, stg, lane);
+                  for (; c0 + 64 <= a.ntok; c0 += 64) store_cols<4>(taddr, c0, dst, M);
                   if (c0 + 32 <= a.ntok) {
-                    stage_cols<2>(taddr, c0, stg, lane);
+                    store_cols<2>(taddr, c0, dst, M);
                     c0 += 32;
                   }
-                  if (c0 < a.ntok) stage_cols<1>(taddr, c0, stg, lane);
+                  if (c0 < a.ntok) store_cols<1>(taddr, c0, dst, M);
                 }
                 tc_fence_before();
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0 && have) {
-                  tma_store_4d(&maps.ps[gi], stg, 32 * (warp & 3), 0, nt, s);
-                  bulk_commit_and_wait();  // written, and the staging rows are free again
-                }
+                fence_proxy_async_global();  // QKV / fc1 partials are read by TMA
                 named_sync(kBarEpi, 128);
-                // each warp's wait_group made its store's writes visible to its
-                // issuing thread, the barrier orders them before the release add
-                // (TMA readers fence their loads)
+                // the barrier orders every epilogue thread's stores before the
+                // release add (TMA readers fence their loads)
                 if (rowred) {
                   if (e == 0) red_release_add(dep + (gi == TG_O ? kDepOp : kDepFc2p), 1u);
                 } else if (e == 0) {
@@ -865,9 +850,8 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
   a.x_bytes = a.ntok * 128;
   a.stage_bytes = kWStageBytes + kKbPerStage * a.x_bytes;  // all sub-tiles multiples of 1 KB (SW128 atoms)
   tp->hd = d / heads;
-  // aux: attention staging, or the partial staging tile (ntok rows) / the S
-  // reduction slices of a QKV or fc1 unit
-  size_t aux_bytes = std::max(attn16_smem_bytes(tp->hd), (size_t)a.ntok * 512);
+  // aux: attention staging, or the S reduction slices of a QKV or fc1 unit
+  size_t aux_bytes = attn16_smem_bytes(tp->hd);
   for (int g : {TG_QKV, TG_FC1}) aux_bytes = std::max(aux_bytes, (size_t)a.S[g] * a.R[g] * 512);
   const size_t budget = 227 * 1024 - 1024 - kBarRegion;
   if (aux_bytes + 2 * (size_t)a.stage_bytes > budget) {
@@ -926,10 +910,6 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
     const uint64_t strides[3] = {512, (uint64_t)M * 512, (uint64_t)M * N[g] * 4};
     const uint32_t box[4] = {128, (uint32_t)a.R[g], 1, (uint32_t)a.S[g]};  // all S slices in one load
     if (encode(&tp->maps.p[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part_g, dims, strides, box,
-               CU_TENSOR_MAP_SWIZZLE_NONE))
-      return -3;
-    const uint32_t sbox[4] = {32, (uint32_t)M, 1, 1};  // one epilogue warp's 32 features
-    if (encode(&tp->maps.ps[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, part_g, dims, strides, sbox,
                CU_TENSOR_MAP_SWIZZLE_NONE))
       return -3;
     a.pslot[g] = part_g;

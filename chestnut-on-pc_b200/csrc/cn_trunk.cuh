@@ -14,7 +14,6 @@ struct TrunkMaps {
   CUtensorMap w[4];  // weights of all layers: [L][KB][N][64] f16, box 64 x 128 x 2 k-blocks
   CUtensorMap x[4];  // GEMM inputs [M][K] f16 as (64, M, K/64), box 64 x ntok x 2 (rows >= M zero-filled)
   CUtensorMap p[4];  // split-K partials [S][N/128][M][128] f32, box 128 x R x 1 x S
-  CUtensorMap ps[4]; // the same partials as a store target, box 32 x M x 1 x 1 (one epilogue warp's features)
 };
 
 struct TrunkArgs {
@@ -25,7 +24,7 @@ struct TrunkArgs {
   int N[4], K[4], S[4], units[4];  // per GEMM slot: features, reduction, split-K, CTAs with work
   int R[4];                        // token rows per split-K reduction slice: ceil(M / S)
   int stages, stage_bytes, x_bytes;
-  int aux_off, bar_off;            // shared-memory layout: ring at 0, then attention / reduction staging
+  int aux_off, bar_off;            // shared-memory layout: ring at 0, then attention / reduction slices
   int phases;                      // grid barriers per launch (1: the closing one)
   float* x;                        // residual stream f32 [M][d]
   __half *h, *qkv, *att, *u;       // LN1 out [M][d], qkv [M][3d], attention out [M][d], MLP hidden [M][mlp]
