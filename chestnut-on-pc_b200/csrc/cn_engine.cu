@@ -122,6 +122,8 @@ struct Step {
   std::string name;
   std::function<int(cudaStream_t)> fn;
   cn_kernel_info info;
+  bool side = false;  // runs on the side stream, forked from the main stream at the first side step
+  bool join = false;  // main step that first waits for everything launched on the side stream
 };
 
 }  // namespace cn
@@ -157,6 +159,10 @@ struct cn_engine {
   size_t tctr_bytes = 0;
   std::vector<Step> steps;
   std::vector<GemmPlan> plans;
+  // side branch of the frame (steps that depend only on the queues, not on the
+  // conv stem) and its fork / join events
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t gexec = nullptr;
   // timed class (event nodes inside the graph)
@@ -348,6 +354,39 @@ static int build_plan(cn_engine* e) {
                         },
                         kinfo("border_gather0", dim3(64, 2 * B + 1), dim3(128), dim3(1, 1, 1), 0)});
   }
+  // Side branch: the cond embedding and the temporal tokens read only what
+  // gather0 wrote, so they run beside the conv stem instead of after it.
+  {
+    GemmParams ep;
+    memset(&ep, 0, sizeof(ep));
+    ep.epi = EPI_F32_OUT;
+    ep.out = e->condv;
+    ep.ldo = m.d;
+    ep.bias = (const float*)wptr(e, "cond.b");
+    CN_TRY(add_gemm(e, "cond", e->cond16, kCondPad, 0, wptr(e, "cond.w"), kCondPad, 0, B, m.d, kCondPad, 1, ep));
+    e->steps.back().side = true;
+    e->plans.back().pdl = false;  // first kernel of the branch: its dependency is the fork event
+  }
+  {
+    // temporal token embeddings into rows [kNVis, kT) of each clip of x
+    GemmParams ep;
+    memset(&ep, 0, sizeof(ep));
+    ep.epi = EPI_TOKENS;
+    ep.out = e->x;
+    ep.ldo = m.d;
+    ep.bias = (const float*)wptr(e, "temp.b");
+    ep.bias_gstride = 0;
+    ep.pos = (const float*)wptr(e, "pos");
+    ep.cond = e->condv;
+    ep.cond_ld = m.d;
+    ep.rows_per_clip = kNTemp;
+    ep.tok_base = kNVis;
+    ep.tok_gstride = 0;
+    ep.T = kT;
+    CN_TRY(add_gemm(e, "temp_tokens", e->feat16, kFeat, 0, wptr(e, "temp.w"), kFeat, 0, B * kNTemp, m.d, kFeat, 1,
+                    ep));
+    e->steps.back().side = true;
+  }
   // conv stem, both cameras as one grouped GEMM per layer
   int cin = 12;
   for (int s = 0; s < 5; ++s) {
@@ -394,17 +433,8 @@ static int build_plan(cn_engine* e) {
     }
     cin = C;
   }
-  // cond embedding (f32, added to every token)
-  {
-    GemmParams ep;
-    memset(&ep, 0, sizeof(ep));
-    ep.epi = EPI_F32_OUT;
-    ep.out = e->condv;
-    ep.ldo = m.d;
-    ep.bias = (const float*)wptr(e, "cond.b");
-    CN_TRY(add_gemm(e, "cond", e->cond16, kCondPad, 0, wptr(e, "cond.w"), kCondPad, 0, B, m.d, kCondPad, 1, ep));
-  }
-  // token embeddings into the residual stream x [B*88][d]
+  // visual token embeddings into the residual stream x [B*88][d]: rows of
+  // the camera tokens; waits for the side branch (cond, temporal tokens)
   {
     GemmParams ep;
     memset(&ep, 0, sizeof(ep));
@@ -423,13 +453,7 @@ static int build_plan(cn_engine* e) {
     const int C4 = m.stem[4];
     CN_TRY(add_gemm(e, "vis_tokens", e->act[4], C4, (long long)B * 32 * C4, wptr(e, "cam0.vis.w"), C4,
                     cam_stride_bytes(e, "cam0.vis.w") / 2, B * 32, m.d, C4, 2, ep));
-    ep.bias = (const float*)wptr(e, "temp.b");
-    ep.bias_gstride = 0;
-    ep.rows_per_clip = kNTemp;
-    ep.tok_base = kNVis;
-    ep.tok_gstride = 0;
-    CN_TRY(add_gemm(e, "temp_tokens", e->feat16, kFeat, 0, wptr(e, "temp.w"), kFeat, 0, B * kNTemp, m.d, kFeat, 1,
-                    ep));
+    e->steps.back().join = true;
   }
   // transformer
   if (e->use_trunk) {
@@ -456,7 +480,7 @@ static int build_plan(cn_engine* e) {
         }
       }
     CN_TRY(trunk_plan(&e->trunk, B, kT, m.d, m.mlp, m.heads, m.layers, w0, wstride, b0, bstride, e->x, e->h, e->qkv,
-                      e->att, e->u, e->h2, e->part, e->tctr, e->rings.ctr, e->nsm));
+                      e->att, e->u, e->h2, e->part, e->tctr, e->rings.ctr, e->nsm, e->h, e->pooled));
     e->steps.push_back({"trunk", [e](cudaStream_t s) { return trunk_launch(e->trunk, s); },
                         kinfo("transformer_trunk", dim3(e->trunk.grid), dim3(256), dim3(1, 1, 1), e->trunk.smem)});
   }
@@ -509,8 +533,9 @@ static int build_plan(cn_engine* e) {
       CN_TRY(add_gemm(e, pre + ".fc2", e->u, m.mlp, 0, wptr(e, pre + ".fc2.w"), m.mlp, 0, R, m.d, m.mlp, 1, ep));
     }
   }
-  {
-    // final LayerNorm (into h) then the token mean of each clip
+  if (!e->use_trunk) {
+    // final LayerNorm (into h) then the token mean of each clip (the
+    // persistent trunk does both at its end)
     float* x = e->x;
     __half* h = e->h;
     __half* p = e->pooled;
@@ -546,19 +571,35 @@ static bool timed(const cn_engine* e, const Step& st) {
 
 static int run_steps(cn_engine* e, cudaStream_t s, bool with_events) {
   size_t ev = 0;
+  bool forked = false;
   for (auto& st : e->steps) {
+    if (st.side && !forked) {  // fork: the side stream starts after the main stream's work so far
+      CN_CUDA(cudaEventRecord(e->ev_fork, s));
+      CN_CUDA(cudaStreamWaitEvent(e->side, e->ev_fork, 0));
+      forked = true;
+    }
+    if (st.join && forked) {  // join: everything on the side stream before this step
+      CN_CUDA(cudaEventRecord(e->ev_join, e->side));
+      CN_CUDA(cudaStreamWaitEvent(s, e->ev_join, 0));
+      forked = false;
+    }
+    const cudaStream_t ss = st.side ? e->side : s;
     const bool t = with_events && timed(e, st);
     // External records become real event-record nodes when captured into the graph.
-    if (t) CN_CUDA(cudaEventRecordWithFlags(e->tev[ev], s, cudaEventRecordExternal));
-    int r = st.fn(s);
+    if (t) CN_CUDA(cudaEventRecordWithFlags(e->tev[ev], ss, cudaEventRecordExternal));
+    int r = st.fn(ss);
     if (r) {
       if (r > 0) set_last_error("launch of %s failed: %s", st.info.name, cudaGetErrorString((cudaError_t)r));
       return r < 0 ? r : CN_ERR_CUDA;
     }
     if (t) {
-      CN_CUDA(cudaEventRecordWithFlags(e->tev[ev + 1], s, cudaEventRecordExternal));
+      CN_CUDA(cudaEventRecordWithFlags(e->tev[ev + 1], ss, cudaEventRecordExternal));
       ev += 2;
     }
+  }
+  if (forked) {  // a branch without a join step rejoins at the end
+    CN_CUDA(cudaEventRecord(e->ev_join, e->side));
+    CN_CUDA(cudaStreamWaitEvent(s, e->ev_join, 0));
   }
   return 0;
 }
@@ -624,6 +665,12 @@ int cn_engine_destroy(cn_engine* e) {
   if (e->gexec) cudaGraphExecDestroy(e->gexec);
   if (e->graph) cudaGraphDestroy(e->graph);
   for (auto ev : e->tev) cudaEventDestroy(ev);
+  if (e->ev_fork) cudaEventDestroy(e->ev_fork);
+  if (e->ev_join) cudaEventDestroy(e->ev_join);
+  if (e->side) {
+    cudaStreamSynchronize(e->side);
+    cudaStreamDestroy(e->side);
+  }
   if (e->wblob) cudaFree(e->wblob);
   if (e->ablob) cudaFree(e->ablob);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -662,8 +709,11 @@ int cn_engine_create(const cn_config* cfg, cn_engine** out) {
       r = CN_ERR_CUDA;
       break;
     }
-    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
-      set_last_error("stream create failed"); r = CN_ERR_CUDA; break;
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming) != cudaSuccess) {
+      set_last_error("stream / event create failed"); r = CN_ERR_CUDA; break;
     }
     // Single-clip frames run the transformer as one persistent kernel;
     // CN_TRUNK=0 selects the per-layer kernels instead.

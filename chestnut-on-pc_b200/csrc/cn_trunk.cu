@@ -776,13 +776,39 @@ __global__ void __launch_bounds__(kTrThreads, 1)
         ok = flags[3] != 0;
       }
     }
-    // the last fc2 brought into x (no LayerNorm follows inside the trunk)
+    // the last fc2 brought into x, and the final LayerNorm of each row into hf
     if (ok && warp >= 4)
       for (int r = blockIdx.x; r < a.M; r += gridDim.x)
         trunk_row<NV>(a, TG_FC2, a.layers - 1, a.dep + (size_t)(a.layers - 1) * kDepPerLayer + kDepFc2p,
-                      (unsigned)a.units[TG_FC2] * ep1, nullptr, r, warp & 3, lane, flags, lnpart);
-    // one grid barrier per launch: every CTA has read the epoch before it moves on
+                      (unsigned)a.units[TG_FC2] * ep1, a.hf, r, warp & 3, lane, flags, lnpart);
+    // one grid barrier per launch: every CTA has read the epoch before it moves
+    // on, and every row of hf is final after it
     if (!grid_sync(a.grid_ctr, (unsigned long long)ep1 * gridDim.x, &flags[0])) ok = false;
+    if (ok && a.pooled) {
+      // token mean of each clip's final LayerNorm rows: a CTA owns 16 clip
+      // columns, thread ct sums row chunk ct / 16 (of 12) of column ct % 16
+      // (the loads of a chunk in flight together), and the 12 chunk sums are
+      // added in chunk order: deterministic, one L2 round trip per chunk
+      constexpr int kPoolCols = 16, kPoolChunks = kComputeThreads / kPoolCols;
+      float* pp = reinterpret_cast<float*>(aux);
+      const int j = ct / kPoolCols, q = ct % kPoolCols;
+      const int t0 = j * a.T / kPoolChunks, t1 = (j + 1) * a.T / kPoolChunks;
+      for (int c0 = blockIdx.x * kPoolCols; c0 < a.B * a.d; c0 += gridDim.x * kPoolCols) {
+        const int b = (c0 + q) / a.d, c = (c0 + q) % a.d;
+        const __half* y = a.hf + (size_t)b * a.T * a.d + c;
+        float sum = 0.f;
+#pragma unroll 8
+        for (int t = t0; t < t1; ++t) sum += __half2float(__ldcg(y + (size_t)t * a.d));
+        pp[j * kPoolCols + q] = sum;
+        named_sync(kBarCompute, kComputeThreads);
+        if (j == 0) {
+          float tot = 0.f;
+          for (int i = 0; i < kPoolChunks; ++i) tot += pp[i * kPoolCols + q];
+          a.pooled[(size_t)b * a.d + c] = __float2half_rn(tot / (float)a.T);
+        }
+        named_sync(kBarCompute, kComputeThreads);
+      }
+    }
     if ((warp == 2 || warp == 3) && lane == 0 && !ok) {
       for (uint32_t i = x_last > (uint32_t)ST ? x_last - ST : 0; i < x_last; ++i)
         if ((int)(i & 1) == warp - 2) mbar_wait(&fullX[i % ST], (i / ST) & 1, 0, 100000000ull);
@@ -836,7 +862,8 @@ size_t trunk_counter_bytes(int layers) {
 
 int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layers, const void* const w0[4],
                long long w_lstride_bytes, const float* const b0[4], long long b_lstride, float* x, __half* h,
-               __half* qkv, __half* att, __half* u, __half* h2, float* part, void* counters, int* bump, int nsm) {
+               __half* qkv, __half* att, __half* u, __half* h2, float* part, void* counters, int* bump, int nsm,
+               __half* hf, __half* pooled) {
   const int M = B * T;
   if (!trunk_supported(M, d, heads) || T > 96 || (mlp % 128) || (d % 128) || mlp / 128 > kMaxTiles ||
       3 * d / 128 > kMaxTiles || (w_lstride_bytes % 16)) {
@@ -901,6 +928,8 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
   a.tile_ctr = reinterpret_cast<unsigned*>(c + 256);
   a.dep = a.tile_ctr + (size_t)layers * 4 * kMaxTiles;
   a.h2 = h2;
+  a.hf = hf;
+  a.pooled = pooled;
   a.bump = bump;
   tp->grid = nsm;
   // tensor maps

@@ -29,6 +29,8 @@ struct TrunkArgs {
   float* x;                        // residual stream f32 [M][d]
   __half *h, *qkv, *att, *u;       // LN1 out [M][d], qkv [M][3d], attention out [M][d], MLP hidden [M][mlp]
   __half* h2;                      // LN2 out [M][d] (its own buffer: LN2 rows overlap QKV steps still reading h)
+  __half* hf;                      // final LayerNorm out [M][d] (may be h: its last reader is done by then)
+  __half* pooled;                  // token mean of hf per clip [B][d], f16 (null: not computed)
   float* part;                     // split-K partials, one [S][N/128][M][128] buffer per GEMM slot
   float* pslot[4];                 // the buffer of each slot
   unsigned* tile_ctr;              // [layers][4][64] split-K arrival counters
@@ -56,7 +58,8 @@ bool trunk_supported(int M, int d, int heads);
 
 int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layers, const void* const w0[4],
                long long w_lstride_bytes, const float* const b0[4], long long b_lstride, float* x, __half* h,
-               __half* qkv, __half* att, __half* u, __half* h2, float* part, void* counters, int* bump, int nsm);
+               __half* qkv, __half* att, __half* u, __half* h2, float* part, void* counters, int* bump, int nsm,
+               __half* hf, __half* pooled);
 int trunk_launch(const TrunkPlan& tp, cudaStream_t s);
 
 }  // namespace cn
