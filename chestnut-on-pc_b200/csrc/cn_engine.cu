@@ -151,6 +151,7 @@ struct cn_engine {
   float *condv, *x, *out;
   // persistent trunk (single-clip frames): split-K partials + counter block
   bool use_trunk = false;
+  bool tail_in_trunk = false;  // the trunk launch also computes hidden state, trunk head and heads
   int nsm = 0;
   TrunkPlan trunk;
   float* part = nullptr;
@@ -481,6 +482,14 @@ static int build_plan(cn_engine* e) {
       }
     CN_TRY(trunk_plan(&e->trunk, B, kT, m.d, m.mlp, m.heads, m.layers, w0, wstride, b0, bstride, e->x, e->h, e->qkv,
                       e->att, e->u, e->h2, e->part, e->tctr, e->rings.ctr, e->nsm, e->h, e->pooled));
+    {
+      // the tail products of the frame run at the end of the trunk launch
+      const void* tw[3] = {wptr(e, "hid.w"), wptr(e, "trunk.w"), wptr(e, "heads.w")};
+      const float* tb[3] = {(const float*)wptr(e, "hid.b"), (const float*)wptr(e, "trunk.b"),
+                            (const float*)wptr(e, "heads.b")};
+      const int tn[3] = {kFeat, kTrunk, kNHeadsOut}, tk[3] = {m.d, kFeat, kTrunk};
+      e->tail_in_trunk = trunk_set_tail(&e->trunk, tw, tb, tn, tk, e->hid16, e->z, e->out, kNHeadsOut);
+    }
     e->steps.push_back({"trunk", [e](cudaStream_t s) { return trunk_launch(e->trunk, s); },
                         kinfo("transformer_trunk", dim3(e->trunk.grid), dim3(256), dim3(1, 1, 1), e->trunk.smem)});
   }
@@ -545,22 +554,25 @@ static int build_plan(cn_engine* e) {
     e->steps.push_back({"pool", [h, p, B, d](cudaStream_t s) { return launch_colmean(h, p, B, kT, d, s, true); },
                         kinfo("token_mean_pool", dim3(B, d / 256), dim3(256), dim3(1, 1, 1), 0)});
   }
-  {
-    GemmParams ep = epi_f16(e->hid16, kFeat, 0, (const float*)wptr(e, "hid.b"), 0, ACT_TANH);
-    ep.out32 = e->out + kNHeadsOut;
-    ep.ld32 = kNOut;
-    CN_TRY(add_gemm(e, "hidden_state", e->pooled, m.d, 0, wptr(e, "hid.w"), m.d, 0, B, kFeat, m.d, 1, ep));
-  }
-  CN_TRY(add_gemm(e, "trunk", e->hid16, kFeat, 0, wptr(e, "trunk.w"), kFeat, 0, B, kTrunk, kFeat, 1,
-                  epi_f16(e->z, kTrunk, 0, (const float*)wptr(e, "trunk.b"), 0, ACT_RELU)));
-  {
-    GemmParams ep;
-    memset(&ep, 0, sizeof(ep));
-    ep.epi = EPI_F32_OUT;
-    ep.out = e->out;
-    ep.ldo = kNOut;
-    ep.bias = (const float*)wptr(e, "heads.b");
-    CN_TRY(add_gemm(e, "heads", e->z, kTrunk, 0, wptr(e, "heads.w"), kTrunk, 0, B, kNHeadsOut, kTrunk, 1, ep));
+  if (!e->tail_in_trunk) {
+    // hidden state, trunk head and heads (the persistent trunk runs them at its end)
+    {
+      GemmParams ep = epi_f16(e->hid16, kFeat, 0, (const float*)wptr(e, "hid.b"), 0, ACT_TANH);
+      ep.out32 = e->out + kNHeadsOut;
+      ep.ld32 = kNOut;
+      CN_TRY(add_gemm(e, "hidden_state", e->pooled, m.d, 0, wptr(e, "hid.w"), m.d, 0, B, kFeat, m.d, 1, ep));
+    }
+    CN_TRY(add_gemm(e, "trunk", e->hid16, kFeat, 0, wptr(e, "trunk.w"), kFeat, 0, B, kTrunk, kFeat, 1,
+                    epi_f16(e->z, kTrunk, 0, (const float*)wptr(e, "trunk.b"), 0, ACT_RELU)));
+    {
+      GemmParams ep;
+      memset(&ep, 0, sizeof(ep));
+      ep.epi = EPI_F32_OUT;
+      ep.out = e->out;
+      ep.ldo = kNOut;
+      ep.bias = (const float*)wptr(e, "heads.b");
+      CN_TRY(add_gemm(e, "heads", e->z, kTrunk, 0, wptr(e, "heads.w"), kTrunk, 0, B, kNHeadsOut, kTrunk, 1, ep));
+    }
   }
   return 0;
 }

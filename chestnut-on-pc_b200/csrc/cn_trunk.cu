@@ -125,6 +125,12 @@ __device__ __forceinline__ void tma_load_4d_hint(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+// Request [p, p + bytes) into L2 (16-byte aligned address and size).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+               : "memory");
+}
+
 // Spin until *ctr >= target (bounded).  false on timeout or a recorded error.
 template <typename T, typename Ld>
 __device__ __forceinline__ bool spin_until(const T* ctr, T target, int code, Ld ld) {
@@ -784,6 +790,15 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     // one grid barrier per launch: every CTA has read the epoch before it moves
     // on, and every row of hf is final after it
     if (!grid_sync(a.grid_ctr, (unsigned long long)ep1 * gridDim.x, &flags[0])) ok = false;
+    if (ok && a.tw[0] && threadIdx.x == kComputeT0) {
+      // this CTA's share of the tail weights into L2 while the pooling runs
+      for (int i = 0; i < 3; ++i) {
+        const size_t bytes = (size_t)a.tN[i] * a.tK[i] * 2, part = (bytes / gridDim.x + 15) & ~size_t(15);
+        const size_t off = part * blockIdx.x;
+        if (off < bytes)
+          bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(a.tw[i]) + off, (uint32_t)min(part, bytes - off));
+      }
+    }
     if (ok && a.pooled) {
       // token mean of each clip's final LayerNorm rows: a CTA owns 16 clip
       // columns, thread ct sums row chunk ct / 16 (of 12) of column ct % 16
@@ -807,6 +822,81 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           a.pooled[(size_t)b * a.d + c] = __float2half_rn(tot / (float)a.T);
         }
         named_sync(kBarCompute, kComputeThreads);
+      }
+      if (threadIdx.x == kComputeT0 && a.tw[0]) red_release_add(a.tail_ctr, 1u);
+    }
+    // tail products: one warp per output (two in flight), lane sums added in a
+    // fixed shuffle tree; phase i starts once every CTA finished phase i - 1
+    if (ok && a.pooled && a.tw[0]) {
+      const int gw = blockIdx.x * (kComputeThreads / 32) + (warp - 2), nw = gridDim.x * (kComputeThreads / 32);
+      for (int tp = 0; tp < 3 && ok; ++tp) {
+        if (threadIdx.x == kComputeT0) flags[2] = spin_until(a.tail_ctr + tp, gridDim.x * ep1, 22, ld_acquire_u32);
+        named_sync(kBarCompute, kComputeThreads);
+        if (flags[2] == 0) {
+          ok = false;
+          break;
+        }
+        const __half* xv = tp == 0 ? a.pooled : (tp == 1 ? a.hid16 : a.z);
+        // lane = (k-block group kq, 16-byte chunk c8): every load instruction of
+        // the warp reads four whole 128-byte k-block rows of one output
+        const int N = a.tN[tp], nv = a.tK[tp] / 256, c8 = lane & 7, kq = lane >> 3;
+        const __half* wb = a.tw[tp] + (size_t)kq * N * 64 + c8 * 8;
+        const size_t wstep = (size_t)4 * N * 64;  // four k-blocks further
+        uint4 xq[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          xq[c] = c < nv ? __ldcg(reinterpret_cast<const uint4*>(xv + (kq + 4 * c) * 64 + c8 * 8))
+                         : make_uint4(0, 0, 0, 0);
+        for (int n0 = gw; n0 < N; n0 += 2 * nw) {
+          float acc[2] = {0.f, 0.f};
+          uint4 wv[2][8];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int n = n0 + j * nw;
+            const __half* wr = wb + (size_t)(n < N ? n : 0) * 64;
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              wv[j][c] = c < nv && n < N ? __ldg(reinterpret_cast<const uint4*>(wr + c * wstep)) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const __half2* wh = reinterpret_cast<const __half2*>(&wv[j][c]);
+              const __half2* xh = reinterpret_cast<const __half2*>(&xq[c]);
+#pragma unroll
+              for (int e2 = 0; e2 < 4; ++e2) {
+                const float2 wf = __half22float2(wh[e2]), xf = __half22float2(xh[e2]);
+                acc[j] = fmaf(wf.x, xf.x, acc[j]);
+                acc[j] = fmaf(wf.y, xf.y, acc[j]);
+              }
+            }
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+          }
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int n = n0 + j * nw;
+            if (lane == 0 && n < N) {
+              const float v = acc[j] + a.tb[tp][n];
+              if (tp == 0) {
+                const __half hv = __float2half_rn(tanhf(v));
+                a.hid16[n] = hv;
+                a.out[a.out_hid + n] = __half2float(hv);
+              } else if (tp == 1) {
+                a.z[n] = __float2half_rn(fmaxf(v, 0.0f));
+              } else {
+                a.out[n] = v;
+              }
+            }
+          }
+        }
+        if (tp < 2) {
+          named_sync(kBarCompute, kComputeThreads);
+          if (threadIdx.x == kComputeT0) red_release_add(a.tail_ctr + tp + 1, 1u);
+        }
       }
     }
     if ((warp == 2 || warp == 3) && lane == 0 && !ok) {
@@ -926,6 +1016,7 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
   a.grid_ctr = reinterpret_cast<unsigned long long*>(c);
   a.epoch = reinterpret_cast<unsigned*>(c + 64);
   a.tile_ctr = reinterpret_cast<unsigned*>(c + 256);
+  a.tail_ctr = reinterpret_cast<unsigned*>(c + 128);
   a.dep = a.tile_ctr + (size_t)layers * 4 * kMaxTiles;
   a.h2 = h2;
   a.hf = hf;
@@ -975,6 +1066,26 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
     return -3;
   }
   return 0;
+}
+
+bool trunk_set_tail(TrunkPlan* tp, const void* const w[3], const float* const b[3], const int N[3], const int K[3],
+                    __half* hid16, __half* z, float* out, int out_hid) {
+  TrunkArgs& a = tp->a;
+  if (a.B != 1 || !a.pooled) return false;
+  for (int i = 0; i < 3; ++i)
+    if (K[i] % 256 || K[i] > 2048 || N[i] < 1 || (reinterpret_cast<uintptr_t>(w[i]) & 15)) return false;
+  if (K[0] != a.d || K[1] != N[0] || K[2] != N[1]) return false;
+  for (int i = 0; i < 3; ++i) {
+    a.tw[i] = static_cast<const __half*>(w[i]);
+    a.tb[i] = b[i];
+    a.tN[i] = N[i];
+    a.tK[i] = K[i];
+  }
+  a.hid16 = hid16;
+  a.z = z;
+  a.out = out;
+  a.out_hid = out_hid;
+  return true;
 }
 
 int trunk_launch(const TrunkPlan& tp, cudaStream_t s) {

@@ -31,6 +31,16 @@ struct TrunkArgs {
   __half* h2;                      // LN2 out [M][d] (its own buffer: LN2 rows overlap QKV steps still reading h)
   __half* hf;                      // final LayerNorm out [M][d] (may be h: its last reader is done by then)
   __half* pooled;                  // token mean of hf per clip [B][d], f16 (null: not computed)
+  // Tail products of a single-clip frame, after the pooling: hidden state
+  // (tanh, f16 + an f32 copy into out), trunk head (relu, f16), heads (f32
+  // into out).  Weights k-blocked [K/64][N][64]; tw[0] null: not computed.
+  const __half* tw[3];
+  const float* tb[3];
+  int tN[3], tK[3];
+  __half *hid16, *z;
+  float* out;
+  int out_hid;          // column of out where the f32 copy of the hidden state starts
+  unsigned* tail_ctr;   // [3] CTAs done with: pooling, hidden state, trunk head
   float* part;                     // split-K partials, one [S][N/128][M][128] buffer per GEMM slot
   float* pslot[4];                 // the buffer of each slot
   unsigned* tile_ctr;              // [layers][4][64] split-K arrival counters
@@ -61,5 +71,9 @@ int trunk_plan(TrunkPlan* tp, int B, int T, int d, int mlp, int heads, int layer
                __half* qkv, __half* att, __half* u, __half* h2, float* part, void* counters, int* bump, int nsm,
                __half* hf, __half* pooled);
 int trunk_launch(const TrunkPlan& tp, cudaStream_t s);
+// Adds the tail products to the launch (batch 1).  Returns false (and leaves
+// the plan unchanged) if a shape is unsupported: K a multiple of 256, <= 2048.
+bool trunk_set_tail(TrunkPlan* tp, const void* const w[3], const float* const b[3], const int N[3], const int K[3],
+                    __half* hid16, __half* z, float* out, int out_hid);
 
 }  // namespace cn

@@ -128,19 +128,22 @@ def test_batched_clips_match_single_clip_engines():
 
 
 def test_kernel_list_describes_the_frame(monkeypatch):
-    # stem 10 + cond/tokens 3 + heads 3 GEMMs, the transformer as one persistent launch
+    # stem 10 + cond/tokens 3 GEMMs; the transformer, the final LayerNorm, the
+    # token mean and the three head products as one persistent launch
     eng = Engine("39m", seed=0)
     ks = eng.kernel_list()
     names = [k["name"] for k in ks]
     assert names[0] == "queue_push" and names[1] == "border_gather0"
-    assert sum(n.startswith("gemm_tc") for n in names) == 10 + 3 + 3
+    assert sum(n.startswith("gemm_tc") for n in names) == 10 + 3
     assert names.count("transformer_trunk") == 1
+    assert "token_mean_pool" not in names and "layernorm:final" not in names
     assert eng.info()["n_kernels"] == len(ks)
-    # per-layer kernels: 4 GEMMs per layer
+    # per-layer kernels: 4 GEMMs per layer, then final LN, pool and 3 head GEMMs
     monkeypatch.setenv("CN_TRUNK", "0")
     names = [k["name"] for k in Engine("39m", seed=0).kernel_list()]
     assert sum(n.startswith("gemm_tc") for n in names) == 10 + 3 + 4 * 4 + 3
     assert "transformer_trunk" not in names
+    assert "token_mean_pool" in names and "layernorm:final" in names
 
 
 def test_persistent_trunk_is_deterministic_and_matches_per_layer_kernels(monkeypatch):
