@@ -65,6 +65,7 @@ _SIGS = {
     "cn_gemm_wmma_f16_noalloc": ([_vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
     "cn_reduce_rows_f16": ([_vp, _vp, _vp, _ll, _ll, _i, _vp], _i),
     "cn_border_gather_s2": ([_vp, _i, _i, _i, _i, _i, _vp, _vp], _i),
+    "cn_warp_frames": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp], _i),
     "cn_device_error": ([ctypes.POINTER(_i)], _i),
     "cn_selftest_bounded_wait": ([_i, ctypes.POINTER(_i)], _i),
     "cn_dev_alloc": ([ctypes.POINTER(_vp), _sz, _i], _i),

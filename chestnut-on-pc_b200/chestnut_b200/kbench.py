@@ -2,6 +2,7 @@
 
     python -m chestnut_b200.kbench gemm   [--bn B --splits S --reps N]
     python -m chestnut_b200.kbench reduce [--cpr C --reps N]
+    python -m chestnut_b200.kbench warp   [--reps N]
 
 The B200 counterpart of the reference's single-kernel A/B benches
 (``bench_r62.py`` for r_6_2_32_4_2_2_2_4_4_384, ``bench_alu.py`` for
@@ -109,9 +110,57 @@ def bench_reduce(cpr=0, reps=10):
                          "peak_source": src, "algorithmic_bytes": byts}}
 
 
+def bench_warp(reps=64, pairs=32):
+    """Frame preparation (cn_warp_frames): road + wide NV12 frames of a 1928 x 1208
+    camera (stride 2048) -> u8[2,6,128,256].  Back-to-back calls in a graph over
+    `pairs` distinct frame pairs (7.5 MB each, more than the L2 in total), so the
+    sampled source bytes come from HBM.  Algorithmic bytes per call: the output
+    (393,216 B) plus one source byte per output byte."""
+    import torch
+    from . import kernels
+    width, height, stride, yh, uvh = 1928, 1208, 2048, 1216, 608
+    fbytes = stride * (yh + uvh)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    frames = torch.randint(0, 256, (pairs, 2, fbytes), device="cuda", generator=g, dtype=torch.uint8)
+    out = torch.empty(2 * 6 * 128 * 256, device="cuda", dtype=torch.uint8)
+    c, s_ = np.cos(0.02), np.sin(0.02)
+    ma = np.array([[3.6 * c, -3.6 * s_, 40.0], [3.6 * s_, 3.6 * c, 300.0], [2e-5, 0.0, 1.0]], np.float32)
+    mb = np.array([[2.1, 0.05, 420.0], [-0.05, 2.1, 350.0], [-3e-5, 0.0, 1.0]], np.float32)
+
+    def call(i, st):
+        kernels.warp_frames(frames[i % pairs, 0].data_ptr(), frames[i % pairs, 1].data_ptr(), ma, mb, width, height,
+                            stride, yh, uvh, out.data_ptr(), stream=st)
+    st = torch.cuda.current_stream().cuda_stream
+    for i in range(3):
+        call(i, st)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        s = torch.cuda.current_stream().cuda_stream
+        for i in range(reps):
+            call(i, s)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(4):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    assert kernels.device_error() == 0
+    us = e0.elapsed_time(e1) * 1e3 / (4 * reps)
+    byts = 2 * 2 * 6 * 128 * 256
+    hbm, tf, src = _peaks()
+    ach = byts / (us * 1e-6) / 1e9
+    return {"kernel": "warp_nv12 (frame preparation, 2 cameras)", "camera": [width, height, stride], "model": [512, 256],
+            "us_per_call": us, "frame_pairs_per_s": 1e6 / us,
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                         "peak_source": src, "algorithmic_bytes": byts}}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("which", choices=["gemm", "reduce"])
+    ap.add_argument("which", choices=["gemm", "reduce", "warp"])
     ap.add_argument("--bn", type=int, default=0)
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--cpr", type=int, default=0)
@@ -120,6 +169,8 @@ def main():
     a = ap.parse_args()
     if a.which == "gemm":
         r = bench_gemm(a.bn, a.splits, a.reps or 50, a.b_kmajor)
+    elif a.which == "warp":
+        r = bench_warp(a.reps or 64)
     else:
         r = bench_reduce(a.cpr, a.reps or 10)
     print(json.dumps(r))

@@ -7,3 +7,4 @@
 #include "cn_attn.cu"
 #include "cn_trunk.cu"
 #include "cn_engine.cu"
+#include "cn_warp.cu"

@@ -23,6 +23,10 @@
  *                         split (run_pinned2.py:989-1066; bench_alu.py:13-16)
  *   cn_border_gather_s2<- the image2d zero-border read (run_pinned2.py:56-92,
  *                         :690-716)
+ *   cn_warp_frames     <- the frame warp warp(tfm, big_tfm, frame, big_frame),
+ *                         compile_modeld.py:179-191 (make_frame_prepare :95-118,
+ *                         warp_perspective_tinygrad :53-81, frames_to_tensor
+ *                         :84-93)
  */
 #ifndef CHESTNUT_H
 #define CHESTNUT_H
@@ -142,6 +146,18 @@ int cn_reduce_rows_f16(const void* x, const void* w, float* out, long long rows,
 /* 3x3 / stride-2 / pad-1 zero-border gather of NHWC f16 [G][B][H][W][C] into
  * f16 [G][B*(H/2)*(W/2)][9*C], k = tap*C + c; C % 8 == 0. */
 int cn_border_gather_s2(const void* act, int G, int B, int H, int W, int C, void* out, void* stream);
+/* Frame preparation: the road (frame) and wide (big_frame) NV12 camera frames,
+ * device u8, each warped with its 3x3 inverse transform (host f32, row-major:
+ * source = M . (x, y, 1)) into the model input u8 [2][6][model_h/2][model_w/2]
+ * on the device (the `warped` layout of cn_run_frame: four 2x2 phases of the
+ * warped Y plane, then U and V at half resolution).  Nearest-neighbour, round
+ * half to even, clipped into the source (no border fill).  NV12 geometry:
+ * stride bytes per row, y_height rows of Y, then uv_height rows of
+ * interleaved UV.  width, height, model_h even; model_w % 8 == 0; out 4-byte
+ * aligned. */
+int cn_warp_frames(const uint8_t* frame, const uint8_t* big_frame, const float* tfm, const float* big_tfm, int width,
+                   int height, int stride, int y_height, int uv_height, int model_w, int model_h, uint8_t* out,
+                   void* stream);
 /* Read (and clear) the device error word. */
 int cn_device_error(int* code);
 /* Failure-detection self-test: launches one CTA that waits on an mbarrier no

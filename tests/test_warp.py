@@ -1,0 +1,145 @@
+"""Frame preparation (NV12 -> 6-plane model input): oracle checks on CPU and
+bit-exact parity of cn_warp_frames with the oracle on the GPU.
+
+The reference's warp (compile_modeld.py:53-118, :179-191) runs in tinygrad,
+which is absent, so parity is against oracle/warp.py's restatement: its
+vectorised form is pinned here against a scalar per-pixel restatement
+(Python's round(), half to even) and against hand-worked cases.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import warp as W
+
+# a camera-sized NV12 buffer: 1928 x 1208, rows padded to 2048 bytes, Y rows
+# padded to 1216, then 608 rows of interleaved UV
+CAM = dict(width=1928, height=1208, stride=2048, y_height=1216, uv_height=608)
+
+
+def _frame(rs, g):
+    return rs.integers(0, 256, g["stride"] * (g["y_height"] + g["uv_height"]), dtype=np.uint8)
+
+
+def _scalar_warp(src, M, w_dst, h_dst):
+    h_src, w_src = src.shape
+    M = np.asarray(M, np.float32).reshape(3, 3)
+    f32 = np.float32
+    out = np.zeros((h_dst, w_dst), np.uint8)
+    for y in range(h_dst):
+        for x in range(w_dst):
+            fx, fy = f32(x), f32(y)
+            s = [f32(f32(f32(M[i, 0] * fx) + f32(M[i, 1] * fy)) + M[i, 2]) for i in range(3)]
+            r = f32(f32(1.0) / s[2])
+            xi = min(max(round(float(f32(s[0] * r))), 0), w_src - 1)
+            yi = min(max(round(float(f32(s[1] * r))), 0), h_src - 1)
+            out[y, x] = src[yi, xi]
+    return out
+
+
+def _calib(scale, rot, persp, tx, ty):
+    c, s = np.cos(rot), np.sin(rot)
+    return np.array([[scale * c, -scale * s, tx], [scale * s, scale * c, ty], [persp, 0.0, 1.0]], np.float32)
+
+
+def test_vectorised_oracle_matches_scalar_restatement():
+    rs = np.random.default_rng(1)
+    src = rs.integers(0, 256, (37, 53), dtype=np.uint8)
+    for M in (_calib(1.7, 0.1, 1e-3, 2.25, -3.5), _calib(0.5, -0.3, -2e-3, 10.0, 4.0),
+              np.array([[1, 0, 0.5], [0, 1, -0.5], [0, 0, 1]], np.float32)):
+        assert np.array_equal(W.warp_perspective(src, M, 24, 16), _scalar_warp(src, M, 24, 16))
+
+
+def test_round_half_to_even_and_clip():
+    src = np.arange(8 * 8, dtype=np.uint8).reshape(8, 8)
+    # x + 0.5: 0.5 -> 0, 1.5 -> 2, 2.5 -> 2, 3.5 -> 4 (half to even); y - 0.5 -> clipped at 0
+    got = W.warp_perspective(src, [[1, 0, 0.5], [0, 1, -0.5], [0, 0, 1]], 4, 2)
+    assert got.tolist() == [[0, 2, 2, 4], [0, 2, 2, 4]]
+    # far outside: every read lands on the clipped corner
+    got = W.warp_perspective(src, [[1, 0, 100], [0, 1, -100], [0, 0, 1]], 3, 3)
+    assert np.all(got == src[0, 7])
+
+
+def test_degenerate_transform_reads_stay_in_the_frame():
+    src = np.arange(16 * 16, dtype=np.uint8).reshape(16, 16)
+    # src_w = 0.01 x - 0.1 crosses zero at x = 10: inf, -inf and NaN coordinates
+    got = W.warp_perspective(src, [[1, 0, 0], [0, 1, 0], [0.01, 0, -0.1]], 16, 4)
+    assert got.shape == (4, 16)
+
+
+def test_frame_prepare_layout_on_a_pure_scale():
+    # M = 2x: model pixel (x, y) reads source (2x, 2y); U / V at half resolution
+    # read (2x, 2y) of their planes too (the UV scaling cancels)
+    g = dict(width=64, height=32, stride=80, y_height=40, uv_height=20)
+    rs = np.random.default_rng(2)
+    f = _frame(rs, g)
+    M = np.diag([2.0, 2.0, 1.0]).astype(np.float32)
+    out = W.frame_prepare(f, M, g["width"], g["height"], g["stride"], g["y_height"], model_w=32, model_h=16)
+    Y, U, V = W.nv12_planes(f, g["width"], g["height"], g["stride"], g["y_height"])
+    yw = Y[0:32:2, 0:64:2]
+    assert np.array_equal(out[0], yw[0::2, 0::2]) and np.array_equal(out[1], yw[1::2, 0::2])
+    assert np.array_equal(out[2], yw[0::2, 1::2]) and np.array_equal(out[3], yw[1::2, 1::2])
+    assert np.array_equal(out[4], U[0:16:2, 0:32:2]) and np.array_equal(out[5], V[0:16:2, 0:32:2])
+    # the UV plane deinterleaves even / odd bytes of the rows after y_height
+    uv0 = g["stride"] * g["y_height"]
+    assert U[1, 3] == f[uv0 + g["stride"] + 6] and V[1, 3] == f[uv0 + g["stride"] + 7]
+
+
+def test_warp_entry_rejects_bad_geometry_without_a_gpu():
+    from chestnut_b200._lib import lib
+    L = lib()
+    m = (ctypes.c_float * 9)(*([1.0] * 9))
+    dummy = ctypes.c_void_p(256)
+    args = dict(width=64, height=32, stride=64, y_height=32, uv_height=16, model_w=32, model_h=16)
+    for bad in (dict(model_w=12), dict(stride=32), dict(width=63), dict(uv_height=8), dict(model_h=15)):
+        a = {**args, **bad}
+        r = L.cn_warp_frames(dummy, dummy, ctypes.addressof(m), ctypes.addressof(m), a["width"], a["height"],
+                             a["stride"], a["y_height"], a["uv_height"], a["model_w"], a["model_h"], dummy, None)
+        assert r == -2, bad
+
+
+# ---------------------------------------------------------------- GPU parity
+def _gpu_warp(fa, fb, Ma, Mb, g, model_w=512, model_h=256):
+    from chestnut_b200 import DeviceBuffer, kernels
+    da, db = DeviceBuffer(fa.nbytes).upload(fa), DeviceBuffer(fb.nbytes).upload(fb)
+    n = 2 * 6 * (model_h // 2) * (model_w // 2)
+    dout = DeviceBuffer(n)
+    kernels.warp_frames(da.ptr, db.ptr, Ma, Mb, g["width"], g["height"], g["stride"], g["y_height"],
+                        g["uv_height"], dout.ptr, model_w, model_h)
+    kernels.synchronize()
+    assert kernels.device_error() == 0
+    return dout.download(np.uint8, (2, 6, model_h // 2, model_w // 2))
+
+
+CASES = {
+    # road / wide camera calibrations: scale to the model image, small roll, a little perspective
+    "calibrated": (_calib(3.6, 0.02, 2e-5, 40.0, 300.0), _calib(2.1, -0.03, -3e-5, 420.0, 350.0)),
+    "half_pixel_ties": (np.array([[2, 0, 0.5], [0, 2, -0.5], [0, 0, 1]], np.float32),
+                        np.array([[3, 0, 1.5], [0, 3, 2.5], [0, 0, 1]], np.float32)),
+    "outside_the_frame": (_calib(1.0, 0.0, 0.0, -5000.0, 9000.0), _calib(50.0, 1.0, 0.0, 0.0, 0.0)),
+    "degenerate_w": (np.array([[1, 0, 0], [0, 1, 0], [0.004, 0, -1]], np.float32),
+                     np.array([[0, 0, 0], [0, 0, 0], [0, 0, 0]], np.float32)),
+}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_gpu_warp_frames_bit_exact(case):
+    rs = np.random.default_rng(3)
+    fa, fb = _frame(rs, CAM), _frame(rs, CAM)
+    Ma, Mb = CASES[case]
+    got = _gpu_warp(fa, fb, Ma, Mb, CAM)
+    ref = W.make_warp(fa, fb, Ma, Mb, CAM["width"], CAM["height"], CAM["stride"], CAM["y_height"])
+    assert np.array_equal(got, ref), int((got != ref).sum())
+
+
+@pytest.mark.gpu
+def test_gpu_warp_frames_small_geometry():
+    g = dict(width=70, height=38, stride=72, y_height=40, uv_height=19)
+    rs = np.random.default_rng(4)
+    fa, fb = _frame(rs, g), _frame(rs, g)
+    Ma, Mb = _calib(2.2, 0.3, 1e-3, 3.0, -2.0), _calib(0.7, -0.2, -5e-3, 30.0, 20.0)
+    got = _gpu_warp(fa, fb, Ma, Mb, g, model_w=40, model_h=22)
+    ref = W.make_warp(fa, fb, Ma, Mb, g["width"], g["height"], g["stride"], g["y_height"], 40, 22)
+    assert np.array_equal(got, ref), int((got != ref).sum())
