@@ -1,8 +1,15 @@
 """ModelState-compatible host class over the B200 engine.
 
 Mirrors ``ModelState.run`` of the reference's openpilot-derived host
-(``modeld.py:165-200``) for callers that already hold the warped frame
-(the NV12 warp, ``compile_modeld.py:53-118``, is not part of this engine):
+(``modeld.py:165-200``).  ``run(bufs, transforms, inputs)`` takes the road
+and wide NV12 camera frames (``bufs['img']``, ``bufs['big_img']``: host
+buffers, or device pointers as ints) and their 3x3 warp transforms, warps
+them on the GPU (``cn_warp_frames``, the reference's ``compile_modeld.py``
+frame warp) into the engine's input and runs the frame from device buffers;
+the NV12 geometry (width, height, stride, y_height, uv_height -- what the
+reference gets from openpilot's ``get_nv12_info``) is given at construction.
+``run(warped, inputs)`` takes an already warped u8[2,6,128,256] frame.
+Both follow the reference's host semantics:
 
   * the desire input is a pulse on the rising edge (modeld.py:177-179):
     ``desire = where(desire_pulse - prev_desire > .99, desire_pulse, 0)`` with
@@ -22,7 +29,7 @@ DESIRE_LEN = 8
 
 
 class ModelState:
-    def __init__(self, model="1b", device=0, seed=0, engine=None):
+    def __init__(self, model="1b", device=0, seed=0, engine=None, nv12=None):
         if engine is None:
             from .engine import Engine
             engine = Engine(model, device=device, batch=1, seed=seed)
@@ -34,12 +41,55 @@ class ModelState:
         }
         self.prev_desire = np.zeros(DESIRE_LEN, dtype=np.float32)
         self.packed = np.zeros(DESIRE_LEN + 2 + 2 + 512, np.float32)  # desire | tc | action_t | prev_feat
+        # NV12 geometry of both cameras: (width, height, stride, y_height, uv_height)
+        self.nv12 = tuple(int(v) for v in nv12) if nv12 is not None else None
+        self._dev = None
 
     def slice_outputs(self, model_outputs, output_slices):
         return {k: model_outputs[np.newaxis, v] for k, v in output_slices.items()}
 
-    def run(self, warped, inputs):
-        """warped u8[2,6,128,256]; inputs: desire_pulse f32[8], traffic_convention f32[2], action_t f32[2]."""
+    def run(self, bufs, transforms, inputs=None):
+        """run(bufs, transforms, inputs): NV12 frames + warp transforms (modeld.py:165);
+        run(warped, inputs): warped u8[2,6,128,256].  inputs: desire_pulse f32[8],
+        traffic_convention f32[2], action_t f32[2]."""
+        if inputs is None:
+            warped, inputs = bufs, transforms
+            return self._run(inputs, lambda p: self.engine.run_frame(warped, p))
+        if self.nv12 is None:
+            raise ValueError("ModelState: NV12 frames need the camera geometry (nv12=...) at construction")
+        return self._run(inputs, lambda p: self._run_nv12(bufs, transforms, p))
+
+    def _buffers(self):
+        if self._dev is None:
+            from ._lib import DeviceBuffer
+            _, _, stride, y_height, uv_height = self.nv12
+            size = stride * (y_height + uv_height)
+            self._dev = {'img': DeviceBuffer(size), 'big_img': DeviceBuffer(size),
+                         'warped': DeviceBuffer(2 * 6 * 128 * 256), 'packed': DeviceBuffer(self.packed.nbytes)}
+        return self._dev
+
+    def _run_nv12(self, bufs, transforms, packed):
+        from . import kernels
+        d = self._buffers()
+        width, height, stride, y_height, uv_height = self.nv12
+        size = stride * (y_height + uv_height)
+        ptr = {}
+        for k in ('img', 'big_img'):
+            b = bufs[k]
+            if isinstance(b, (int, np.integer)):
+                ptr[k] = int(b)          # already on the device (the caller's frame buffer)
+            else:
+                a = np.frombuffer(memoryview(b).cast('B'), np.uint8) if not isinstance(b, np.ndarray) else b
+                d[k].upload(np.ascontiguousarray(a.reshape(-1)[:size]))
+                ptr[k] = d[k].ptr
+        # warp on the engine's stream, then the frame from device buffers (same stream)
+        kernels.warp_frames(ptr['img'], ptr['big_img'], transforms['img'], transforms['big_img'], width, height,
+                            stride, y_height, uv_height, d['warped'].ptr, stream=self.engine.stream_handle())
+        d['packed'].upload(packed)
+        self.engine.run_frame_device(d['warped'].ptr, d['packed'].ptr)
+        return self.engine.read_output()[0]
+
+    def _run(self, inputs, frame):
         desire_pulse = np.asarray(inputs['desire_pulse'], np.float32).reshape(-1).copy()
         desire_pulse[0] = 0
         desire = np.where(desire_pulse - self.prev_desire > .99, desire_pulse, 0)
@@ -48,7 +98,7 @@ class ModelState:
         p[0:8] = desire
         p[8:10] = np.asarray(inputs['traffic_convention'], np.float32).reshape(-1)
         p[10:12] = np.asarray(inputs['action_t'], np.float32).reshape(-1)
-        out = np.asarray(self.engine.run_frame(warped, p)).reshape(-1)
+        out = np.asarray(frame(p)).reshape(-1)
         if not np.all(np.isfinite(out)):
             return None
         self.packed[:12] = p[:12]

@@ -143,3 +143,42 @@ def test_gpu_warp_frames_small_geometry():
     got = _gpu_warp(fa, fb, Ma, Mb, g, model_w=40, model_h=22)
     ref = W.make_warp(fa, fb, Ma, Mb, g["width"], g["height"], g["stride"], g["y_height"], 40, 22)
     assert np.array_equal(got, ref), int((got != ref).sum())
+
+
+def test_modelstate_nv12_needs_the_camera_geometry():
+    from chestnut_b200.modeld import ModelState
+
+    class NoEngine:
+        out_slices = {}
+    ms = ModelState(engine=NoEngine())
+    inputs = {"desire_pulse": np.zeros(8, np.float32), "traffic_convention": np.zeros(2, np.float32),
+              "action_t": np.zeros(2, np.float32)}
+    with pytest.raises(ValueError):
+        ms.run({"img": b"", "big_img": b""}, {"img": np.eye(3), "big_img": np.eye(3)}, inputs)
+
+
+@pytest.mark.gpu
+def test_gpu_modelstate_nv12_frames_equal_the_warped_path():
+    # ModelState.run(bufs, transforms, inputs) (GPU warp + device frame) against
+    # the oracle's warp fed to ModelState.run(warped, inputs) on a second engine:
+    # the same warped bytes reach the same deterministic frame, so outputs and
+    # the carried hidden state agree bit for bit over several frames
+    from chestnut_b200 import Engine
+    from chestnut_b200.modeld import ModelState
+    g = CAM
+    geom = (g["width"], g["height"], g["stride"], g["y_height"], g["uv_height"])
+    a = ModelState(engine=Engine("39m", seed=3), nv12=geom)
+    b = ModelState(engine=Engine("39m", seed=3))
+    rs = np.random.default_rng(5)
+    tf = {"img": _calib(3.6, 0.02, 2e-5, 40.0, 300.0), "big_img": _calib(2.1, -0.03, -3e-5, 420.0, 350.0)}
+    for f in range(3):
+        fa, fb = _frame(rs, g), _frame(rs, g)
+        d = np.zeros(8, np.float32)
+        d[f % 8] = 1.0
+        inputs = {"desire_pulse": d, "traffic_convention": np.array([1.0, 0.0], np.float32),
+                  "action_t": np.array([0.1 * f, 0.0], np.float32)}
+        oa = a.run({"img": fa, "big_img": fb}, tf, dict(inputs))
+        warped = W.make_warp(fa, fb, tf["img"], tf["big_img"], g["width"], g["height"], g["stride"], g["y_height"])
+        ob = b.run(warped, dict(inputs))
+        for k in oa:
+            assert np.array_equal(oa[k], ob[k]), (f, k)
