@@ -31,7 +31,7 @@ sys.path.insert(0, os.path.join(ROOT, "chestnut-on-pc_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "1B-model frame latency p50 ms (1×B200); clip frames/s at 1/2/4/8 GPUs"
-PUBLISHED_MS = 84.0        # 1B frame on RTX 2080 (README.md:19,39)
+PUBLISHED_MS = 84.0        # the reference's published 1B frame time on an RTX 2080 (README.md:19,39)
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 
 

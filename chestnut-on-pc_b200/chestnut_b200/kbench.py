@@ -13,7 +13,7 @@ and a one-line JSON report with the roofline fraction.
 * gemm: C f32[768x256] += A f16[768x6144] x B f16[6144x256] (B as [K][N], the
   BASELINE layout), A, B ~ N(0,1)/sqrt(6144).  Back-to-back launches captured
   in a CUDA graph (launch latency exceeds the kernel), operands L2-warm: the
-  tensor roofline is the judged one (2.416 GFLOP per call).
+  tensor roofline is the one that bounds it (2.416 GFLOP per call).
 * reduce: out f32[3072] = x f16[3072x393216] . w f16[393216], U(-1,1).  The L2
   is flushed between launches (x is 2.4 GB anyway): HBM roofline, 2,416,717,824
   algorithmic bytes per call.
