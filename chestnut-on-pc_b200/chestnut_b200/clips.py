@@ -4,11 +4,16 @@ Independent clips -- each with its own recurrent state (queues + hidden state)
 -- are the only axis the frame path shards on: clip c runs on rank c % world,
 ``batch`` clips per engine launch.  No collective runs on the per-frame path;
 each rank's per-clip results are gathered to every rank (rank 0 reports) once,
-at clip end, with ``torch.distributed`` (NCCL over NVLink on GPUs, gloo on CPU).
-The reference has no multi-GPU path; this follows the clip-parallel plan of its
+at clip end, through a transport: ``NcclGather`` drives NCCL from C++
+(libcncomm.so, include/chestnut_comm.h) over NVLink; anything with the same
+``allgather`` method (a test's gloo transport, say) works too.  The reference
+has no multi-GPU path; this follows the clip-parallel plan of its
 ``video_check.py:50-94`` loop (per clip: frames -> run_frame -> carried hidden
-state -> per-frame rows).
+state -> per-frame rows).  No PyTorch here.
 """
+import ctypes
+import os
+
 import numpy as np
 
 
@@ -61,28 +66,99 @@ def run_rank(engine_factory, frame_source, clips, n_frames, batch, batch_source=
     return results
 
 
-def gather(results, n_clips, n_frames, n_out, dist, device=None):
+class CommError(RuntimeError):
+    pass
+
+
+_COMM = None
+
+
+def comm_lib():
+    """libcncomm.so (ctypes); raises CommError if it is missing."""
+    global _COMM
+    if _COMM is None:
+        path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libcncomm.so")
+        if not os.path.exists(path):
+            raise CommError(f"{path} is missing: build it with chestnut-on-pc_b200/build.py")
+        L = ctypes.CDLL(path)
+        vp, i, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+        sigs = {"cn_comm_last_error": ([], ctypes.c_char_p), "cn_comm_nccl_version": ([ctypes.POINTER(i)], i),
+                "cn_comm_unique_id": ([vp], i), "cn_comm_init": ([ctypes.POINTER(vp), i, i, i, vp, i], i),
+                "cn_comm_allgather_f64": ([vp, vp, vp, sz, i], i), "cn_comm_destroy": ([vp], i)}
+        for name, (args, res) in sigs.items():
+            f = getattr(L, name)
+            f.argtypes, f.restype = args, res
+        _COMM = L
+    return _COMM
+
+
+ID_BYTES = 128
+
+
+def _check(rc, what):
+    if rc != 0:
+        raise CommError(f"{what} failed ({rc}): {comm_lib().cn_comm_last_error().decode(errors='replace')}")
+
+
+class NcclGather:
+    """Clip-end all-gather over NCCL, driven from C++ (one process per GPU).
+
+    ``unique_id``: the CN_COMM_ID_BYTES rendezvous bytes made on rank 0 by
+    ``NcclGather.new_id()`` and handed to every rank by the host's own
+    launcher (a key-value store, a broadcast, a file).  A rank that does not
+    arrive within ``timeout_s`` turns into a CommError instead of a hang.
+    """
+
+    def __init__(self, rank, world, device, unique_id, timeout_s=60.0):
+        if len(unique_id) != ID_BYTES:
+            raise CommError(f"unique id must be {ID_BYTES} bytes")
+        self.world, self.rank = int(world), int(rank)
+        self.timeout_ms = int(timeout_s * 1000)
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(unique_id), ID_BYTES)
+        _check(comm_lib().cn_comm_init(ctypes.byref(h), int(device), self.world, self.rank, buf, self.timeout_ms),
+               "cn_comm_init")
+        self._h = h
+
+    @staticmethod
+    def new_id():
+        buf = ctypes.create_string_buffer(ID_BYTES)
+        _check(comm_lib().cn_comm_unique_id(buf), "cn_comm_unique_id")
+        return buf.raw
+
+    def allgather(self, arr):
+        """f64 array on every rank -> f64 [world, *arr.shape], rank r's array in row r."""
+        a = np.ascontiguousarray(arr, np.float64)
+        out = np.empty((self.world,) + a.shape, np.float64)
+        _check(comm_lib().cn_comm_allgather_f64(self._h, a.ctypes.data, out.ctypes.data, a.size, self.timeout_ms),
+               "cn_comm_allgather_f64")
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            comm_lib().cn_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def gather(results, n_clips, n_frames, n_out, transport=None):
     """All-gather every rank's per-clip results (one collective, at clip end).
 
     Returns (checksums f64[n_clips, n_frames], finals f32[n_clips, n_out]) on
     every rank.  Clips a rank does not own are zero in its contribution, so the
-    gather is a sum over ranks of disjoint rows.
+    gather is a sum over ranks of disjoint rows (exact: every row has one
+    non-zero contributor).  ``transport`` None means a single process.
     """
-    import torch
-
     local_s = np.zeros((n_clips, n_frames), np.float64)
     local_f = np.zeros((n_clips, n_out), np.float64)
     for c, (s, f) in results.items():
         local_s[c] = s
         local_f[c] = f
-    packed = torch.from_numpy(np.concatenate([local_s, local_f], axis=1))
-    if device is not None:
-        packed = packed.to(device)
-    if dist is not None and dist.is_initialized() and dist.get_world_size() > 1:
-        parts = [torch.zeros_like(packed) for _ in range(dist.get_world_size())]
-        dist.all_gather(parts, packed)
-        total = torch.stack(parts).sum(0)
-    else:
-        total = packed
-    total = total.cpu().numpy()
+    packed = np.concatenate([local_s, local_f], axis=1)
+    total = transport.allgather(packed).sum(0) if transport is not None else packed
     return total[:, :n_frames], total[:, n_frames:].astype(np.float32)

@@ -38,6 +38,10 @@ constexpr int kNaStages = 4;
 constexpr int kNaTile = 128 * 64 * 2;  // one 128-row x 64-k f16 tile (A or B)
 constexpr int kNaStage = 2 * kNaTile;
 constexpr int kNaMaxSplits = 16;
+// Barrier area after the stage buffers: full[kNaStages], empty[kNaStages],
+// done (8 bytes each), then the TMEM slot and the last-arriver flag (4 each).
+constexpr int kNaBarBytes = (2 * kNaStages + 1) * 8 + 2 * 4;
+static_assert(kNaBarBytes <= 128, "barrier area of the no-alloc GEMM");
 
 struct NoallocArgs {
   int M, N, K, S;
@@ -173,7 +177,9 @@ __global__ void __launch_bounds__(kNaThreads, 1)
       }
     }
   }
-  // error path: no TMA write may still be in flight when the CTA exits
+  // Error path: no TMA write may still be in flight when the CTA exits.  Best
+  // effort: if this bounded drain also runs out, the error is already recorded
+  // and the CTA exits anyway (as in cn_gemm.cu).
   if (warp == 0 && lane == 0 && g_cn_dev_error != 0)
     for (int i = (issued > kNaStages ? issued - kNaStages : 0); i < issued; ++i)
       mbar_wait(&full[i % kNaStages], (i / kNaStages) & 1, 0, 100000000ull);
@@ -182,7 +188,8 @@ __global__ void __launch_bounds__(kNaThreads, 1)
   if (warp == 2) tmem_dealloc(tmem, 128);
 }
 
-size_t noalloc_smem_bytes() { return (size_t)kNaStages * kNaStage + 64 + 1024; }
+// stage buffers + the barrier area rounded up to 128 bytes + 1024 bytes of alignment slack
+size_t noalloc_smem_bytes() { return (size_t)kNaStages * kNaStage + 128 + 1024; }
 
 }  // namespace
 
@@ -204,11 +211,18 @@ extern "C" int cn_gemm_wmma_f16_noalloc(const void* A, const void* B, float* C, 
   }
   const int tm = (M + 127) / 128, tn = (N + 127) / 128;
   const size_t Mp = (size_t)tm * 128, Np = (size_t)tn * 128;
+  // Scratch is used only with splits > 1: one arrival counter per output tile
+  // (at most 1024 tiles) and S partial tiles.  splits == 1 needs none.
   const size_t part_bytes = splits > 1 ? (size_t)splits * Mp * Np * 4 : 0;
-  if ((size_t)tm * tn * 4 > kNoallocCounterBytes || kNoallocCounterBytes + part_bytes > kNoallocScratchBytes) {
+  if (splits > 1 && (size_t)tm * tn * 4 > kNoallocCounterBytes) {
+    set_last_error("cn_gemm_wmma_f16_noalloc: %d x %d output tiles exceed the tile limit of the static scratch "
+                   "(at most 1024 output tiles when splits > 1)", tm, tn);
+    return -2;
+  }
+  if (splits > 1 && kNoallocCounterBytes + part_bytes > kNoallocScratchBytes) {
     set_last_error("cn_gemm_wmma_f16_noalloc: %d x %d tiles x %d splits need %zu bytes of scratch; the static "
-                   "scratch holds %zu bytes (at most 1024 output tiles)", tm, tn, splits,
-                   kNoallocCounterBytes + part_bytes, kNoallocScratchBytes);
+                   "scratch holds %zu bytes", tm, tn, splits, kNoallocCounterBytes + part_bytes,
+                   kNoallocScratchBytes);
     return -2;
   }
   // Set-up, once per device with that device current: the device address of

@@ -132,8 +132,9 @@ int cn_gemm_wmma_f16(const void* A, const void* B, float* C, int M, int N, int K
  * synchronisation is not allowed).  No counterpart in the reference.  The
  * split-K partial tiles and tile counters live in a 16 MiB static device array
  * that every GPU loading the library holds until exit; calls needing more
- * (splits x M x N rounded up to 128, x 4 bytes, plus 4 KiB of counters) or more
- * than 1024 output tiles are rejected with CN_ERR_ARG.  splits in [1, 16] and
+ * (splits x M x N rounded up to 128, x 4 bytes, plus 4 KiB of counters) or, with
+ * splits > 1, more than 1024 output tiles are rejected with CN_ERR_ARG
+ * (splits = 1 uses no scratch).  splits in [1, 16] and
  * <= ceil(K/64).  The first call on a device looks up the array's device
  * address, so make it before any stream capture.  All calls share the array:
  * calls that overlap on the GPU race. */

@@ -2,7 +2,10 @@
 
 A fake engine stands in for the GPU: it is a deterministic function of the
 frame inputs and the carried hidden state, so a sharded run must reproduce the
-single-process run bit for bit.
+single-process run bit for bit.  The clip-end gather goes through a gloo
+transport with the same ``allgather`` contract as clips.NcclGather (which
+needs GPUs); the NCCL library itself is checked for its exports and its
+argument errors here, and run for real by the multi-GPU bench.
 """
 import os
 import socket
@@ -54,6 +57,20 @@ def _free_port():
         return s.getsockname()[1]
 
 
+class GlooTransport:
+    """clips.NcclGather's allgather contract over a gloo process group."""
+
+    def __init__(self, dist):
+        self.dist = dist
+
+    def allgather(self, arr):
+        import torch
+        t = torch.from_numpy(np.ascontiguousarray(arr, np.float64))
+        parts = [torch.zeros_like(t) for _ in range(self.dist.get_world_size())]
+        self.dist.all_gather(parts, t)
+        return torch.stack(parts).numpy()
+
+
 def _rank_main(rank, world, port, n_clips, n_frames, batch, out_path):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -61,7 +78,7 @@ def _rank_main(rank, world, port, n_clips, n_frames, batch, out_path):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     mine = clips.assign(n_clips, world, rank)
     res = clips.run_rank(FakeEngine, frame_source, mine, n_frames, batch)
-    sums, finals = clips.gather(res, n_clips, n_frames, N_OUT, dist)
+    sums, finals = clips.gather(res, n_clips, n_frames, N_OUT, GlooTransport(dist))
     if rank == 0:
         np.savez(out_path, sums=sums, finals=finals)
     dist.barrier()
@@ -92,3 +109,22 @@ def test_batching_does_not_change_results():
     b = clips.run_rank(FakeEngine, frame_source, [0, 1, 2], 3, 3)
     for c in (0, 1, 2):
         assert np.array_equal(a[c][0], b[c][0]) and np.array_equal(a[c][1], b[c][1])
+
+
+def test_comm_library_exports_and_argument_errors():
+    import ctypes
+    from chestnut_b200.clips import comm_lib
+    L = comm_lib()
+    v = ctypes.c_int(0)
+    assert L.cn_comm_nccl_version(ctypes.byref(v)) == 0 and v.value >= 22000
+    assert L.cn_comm_unique_id(None) == -2
+    h = ctypes.c_void_p()
+    assert L.cn_comm_init(ctypes.byref(h), 0, 2, 5, b"x" * 128, 1000) == -2   # rank outside [0, nranks)
+    assert b"bad arguments" in L.cn_comm_last_error()
+    assert L.cn_comm_allgather_f64(None, None, None, 1, 1000) == -2
+    assert L.cn_comm_destroy(None) == 0
+    hdr = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                            "chestnut_comm.h")).read()
+    import re
+    for name in re.findall(r"^int (cn_comm_\w+)\(", hdr, re.M):
+        assert hasattr(L, name), name

@@ -54,4 +54,7 @@ def test_noalloc_gemm_refuses_sizes_beyond_its_static_scratch():
     # 4096 x 4096 output x 16 splits needs 1 GiB of partial tiles
     assert L.cn_gemm_wmma_f16_noalloc(a.ptr, a.ptr, a.ptr, 4096, 4096, 4096, 16, None) == CN_ERR_ARG
     assert b"static scratch" in L.cn_last_error()
+    # 33 x 33 = 1089 output tiles with splits > 1: more tiles than the scratch has counters
+    assert L.cn_gemm_wmma_f16_noalloc(a.ptr, a.ptr, a.ptr, 4224, 4224, 128, 2, None) == CN_ERR_ARG
+    assert b"tile limit" in L.cn_last_error()
     assert L.cn_gemm_wmma_f16_noalloc(a.ptr, a.ptr, a.ptr, 128, 128, 64, 2, None) == CN_ERR_ARG  # splits > K/64
