@@ -33,6 +33,11 @@ class cn_slice(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 16), ("start", ctypes.c_int), ("stop", ctypes.c_int)]
 
 
+class cn_decode_field(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int), ("raw_off", ctypes.c_int), ("raw_len", ctypes.c_int), ("in_n", ctypes.c_int),
+                ("out_n", ctypes.c_int), ("width", ctypes.c_int), ("out_off", ctypes.c_int)]
+
+
 class ChestnutError(RuntimeError):
     pass
 
@@ -66,6 +71,9 @@ _SIGS = {
     "cn_reduce_rows_f16": ([_vp, _vp, _vp, _ll, _ll, _i, _vp], _i),
     "cn_border_gather_s2": ([_vp, _i, _i, _i, _i, _i, _vp, _vp], _i),
     "cn_warp_frames": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp], _i),
+    "cn_decode_layout": ([ctypes.POINTER(cn_decode_field), _i, ctypes.POINTER(_i)], _i),
+    "cn_decode_outputs": ([_vp, _i, _i, ctypes.POINTER(cn_decode_field), _i, _vp, _i, _vp], _i),
+    "cn_decode_frame": ([_vp, ctypes.POINTER(cn_decode_field), _i, _vp], _i),
     "cn_device_error": ([ctypes.POINTER(_i)], _i),
     "cn_selftest_bounded_wait": ([_i, ctypes.POINTER(_i)], _i),
     "cn_dev_alloc": ([ctypes.POINTER(_vp), _sz, _i], _i),

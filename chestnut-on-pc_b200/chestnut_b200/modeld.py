@@ -19,9 +19,12 @@ Both follow the reference's host semantics:
     modeld.py:191-194) and does not update the carried features;
   * ``prev_feat`` is carried from ``out[hidden_state]`` (modeld.py:196).
 
-Output decoding (``parse_model_outputs.Parser``) is not part of the hot path;
 ``run`` returns the sliced heads the way ``slice_outputs`` does
-(``modeld.py:160-162``), each with a leading batch axis.
+(``modeld.py:160-162``), each with a leading batch axis.  Given a decode
+layout at construction (``decode=SYNTHETIC_LAYOUT`` or a real model's), the
+frame output is also parsed on the GPU as ``parse_model_outputs.Parser``
+would parse it on the host (``decode.py``), and the parsed keys are added to
+the returned dict with the same leading batch axis.
 """
 import numpy as np
 
@@ -29,7 +32,7 @@ DESIRE_LEN = 8
 
 
 class ModelState:
-    def __init__(self, model="1b", device=0, seed=0, engine=None, nv12=None):
+    def __init__(self, model="1b", device=0, seed=0, engine=None, nv12=None, decode=None):
         if engine is None:
             from .engine import Engine
             engine = Engine(model, device=device, batch=1, seed=seed)
@@ -45,6 +48,7 @@ class ModelState:
         self.nv12 = tuple(int(v) for v in nv12) if nv12 is not None else None
         self._dev = None
         self.last_output = None
+        self.decode_layout = decode
 
     def slice_outputs(self, model_outputs, output_slices):
         return {k: model_outputs[np.newaxis, v] for k, v in output_slices.items()}
@@ -105,4 +109,9 @@ class ModelState:
             return None
         self.packed[:12] = p[:12]
         self.packed[12:] = out[self.output_slices['hidden_state']]
-        return self.slice_outputs(out, self.output_slices)
+        res = self.slice_outputs(out, self.output_slices)
+        if self.decode_layout is not None:
+            from .decode import decode_frame
+            for k, v in decode_frame(self.engine, self.decode_layout)[0].items():
+                res[k] = v[np.newaxis]
+        return res

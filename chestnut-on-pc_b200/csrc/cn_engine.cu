@@ -170,6 +170,8 @@ struct cn_engine {
   std::string timed_prefix;
   std::vector<cudaEvent_t> tev;  // pairs
   int pending = 0;               // a frame is in flight
+  float* dec = nullptr;          // decoded outputs (cn_decode_frame), allocated on first use
+  size_t dec_floats = 0;
 };
 
 namespace cn {
@@ -685,6 +687,7 @@ int cn_engine_destroy(cn_engine* e) {
   }
   if (e->wblob) cudaFree(e->wblob);
   if (e->ablob) cudaFree(e->ablob);
+  if (e->dec) cudaFree(e->dec);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
   return 0;
@@ -778,6 +781,28 @@ int cn_read_output(cn_engine* e, float* out) {
   if (!e || !out) return CN_ERR_ARG;
   CN_CUDA(cudaSetDevice(e->cfg.device));
   CN_CUDA(cudaMemcpyAsync(out, e->out, (size_t)e->B * kNOut * 4, cudaMemcpyDeviceToHost, e->stream));
+  return cn_sync(e);
+}
+
+int cn_decode_frame(cn_engine* e, const cn_decode_field* fields, int n_fields, float* host_out) {
+  if (!e || !fields || !host_out || n_fields < 1 || n_fields > 32) {
+    set_last_error("cn_decode_frame: bad arguments");
+    return CN_ERR_ARG;
+  }
+  std::vector<cn_decode_field> f(fields, fields + n_fields);
+  int len = 0;
+  CN_TRY(cn_decode_layout(f.data(), n_fields, &len));
+  CN_CUDA(cudaSetDevice(e->cfg.device));
+  const size_t need = (size_t)e->B * len;
+  if (need > e->dec_floats) {
+    if (e->dec) CN_CUDA(cudaFree(e->dec));
+    e->dec = nullptr;
+    e->dec_floats = 0;
+    CN_CUDA(cudaMalloc(&e->dec, need * 4));
+    e->dec_floats = need;
+  }
+  CN_TRY(cn_decode_outputs(e->out, e->B, kNOut, f.data(), n_fields, e->dec, len, e->stream));
+  CN_CUDA(cudaMemcpyAsync(host_out, e->dec, need * 4, cudaMemcpyDeviceToHost, e->stream));
   return cn_sync(e);
 }
 

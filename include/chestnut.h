@@ -27,6 +27,11 @@
  *                         compile_modeld.py:179-191 (make_frame_prepare :95-118,
  *                         warp_perspective_tinygrad :53-81, frames_to_tensor
  *                         :84-93)
+ *   cn_decode_outputs /
+ *   cn_decode_frame    <- the host-side output parser Parser.parse_outputs
+ *                         (parse_model_outputs.py:1-120: parse_mdn,
+ *                         parse_binary_crossentropy,
+ *                         parse_categorical_crossentropy), on the GPU
  */
 #ifndef CHESTNUT_H
 #define CHESTNUT_H
@@ -159,6 +164,38 @@ int cn_border_gather_s2(const void* act, int G, int B, int H, int W, int C, void
 int cn_warp_frames(const uint8_t* frame, const uint8_t* big_frame, const float* tfm, const float* big_tfm, int width,
                    int height, int stride, int y_height, int uv_height, int model_w, int model_h, uint8_t* out,
                    void* stream);
+/* ---- output decode (parse_model_outputs.py:1-120 on the GPU) ----------
+ * A layout lists fields of one frame's raw output vector.  MDN
+ * (Parser.parse_mdn): max(in_n,1) hypothesis rows [mu n | log-std n | ... |
+ * out_n selection logits], std = exp(min(x, 11)); in_n > 1 needs out_n >= 1
+ * (weights = softmax across hypotheses per selection column; out_n == 1
+ * reorders the hypotheses by weight, descending), in_n <= 1 needs out_n == 0.
+ * Decoded per MDN field: [weights in_n*out_n | mu in_n*n | std in_n*n] (in_n
+ * > 1 only), then [mu | std] of the best hypothesis per column (max(out_n,1)
+ * x n each).  SIGMOID: 1 / (1 + exp(min(-x, 11))).  SOFTMAX: softmax over
+ * consecutive groups of `width` values.  At most 32 fields, 64 hypotheses and
+ * 8 selection columns. */
+#define CN_DECODE_MDN 0
+#define CN_DECODE_SIGMOID 1
+#define CN_DECODE_SOFTMAX 2
+typedef struct cn_decode_field {
+  int kind;              /* CN_DECODE_* */
+  int raw_off, raw_len;  /* the field's values in one frame's raw vector */
+  int in_n, out_n;       /* MDN: parse_mdn's in_N (hypotheses) and out_N (selection columns) */
+  int width;             /* SOFTMAX: values per group */
+  int out_off;           /* set by cn_decode_layout: first decoded value in one frame's output */
+} cn_decode_field;
+/* Checks a layout, sets every field's out_off and the decoded floats per frame. */
+int cn_decode_layout(cn_decode_field* fields, int n_fields, int* out_len);
+/* raw: device f32 [batch][raw_stride]; out: device f32 [batch][out_stride]
+ * (fields as returned by cn_decode_layout). */
+int cn_decode_outputs(const float* raw, int batch, int raw_stride, const cn_decode_field* fields, int n_fields,
+                      float* out, int out_stride, void* stream);
+/* Decode the engine's last frame output on its stream (after cn_run_frame /
+ * cn_run_frame_device) and copy the decoded values to host f32
+ * [batch][out_len], out_len from cn_decode_layout.  Synchronous. */
+int cn_decode_frame(cn_engine* e, const cn_decode_field* fields, int n_fields, float* host_out);
+
 /* Read (and clear) the device error word. */
 int cn_device_error(int* code);
 /* Failure-detection self-test: launches one CTA that waits on an mbarrier no
