@@ -219,13 +219,14 @@ def bench_gemm(reps=50, bn=0, splits=0, b_kmajor=0):
             "hbm_view": {"algorithmic_bytes": byts, "frac_of_hbm": byts / (us * 1e-6) / 1e9 / hbm}}
 
 
-def bench_reduce(reps=10, cpr=0):
+def bench_reduce(reps=10, cpr=0, rows=32 * 32 * 3):
     """Config 2: out f32[3072] = x f16[3072x393216] . w f16[393216], U(-1,1).  The
     L2 is flushed between launches (x is 2.4 GB anyway): HBM roofline,
-    2,416,717,824 algorithmic bytes per call."""
+    2,416,717,824 algorithmic bytes per call.  `rows` < 3072 runs a smaller case
+    of the same kernel (profiling)."""
     import torch
     from chestnut_b200 import kernels
-    rows, L = 32 * 32 * 3, 12288 * 32
+    L = 12288 * 32
     g = torch.Generator(device="cuda").manual_seed(0)
     x = (torch.rand(rows * L, device="cuda", generator=g, dtype=torch.float16) * 2 - 1)
     w = (torch.rand(L, device="cuda", generator=g, dtype=torch.float16) * 2 - 1)
@@ -729,6 +730,7 @@ def main():
     ap.add_argument("--bn", type=int, default=0)
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--reps", type=int, default=0)
+    ap.add_argument("--reduce-rows", type=int, default=3072, help="rows of the --kernel reduce case")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -740,7 +742,7 @@ def main():
         if args.kernel == "gemm":
             line = bench_gemm(args.reps or 50, args.bn, args.splits)
         elif args.kernel == "reduce":
-            line = bench_reduce(args.reps or 10)
+            line = bench_reduce(args.reps or 10, rows=args.reduce_rows)
         elif args.kernel == "warp":
             line = bench_warp(args.reps or 64)
         else:

@@ -325,8 +325,9 @@ __device__ __forceinline__ bool trunk_row(const TrunkArgs& a, int src, int sl, c
 
 // Attention of query rows [q0, q0 + 16) of (clip b, head h).  Shared layout
 // (halves, row stride HD + 8): Q rows 0..15, K rows 16..111, V rows 112..207.
-constexpr int kAttnKW = 32;                  // keys per warp
-constexpr int kAttnWarpsT = kAttnRows / kAttnKW;  // 3 warps split the keys
+constexpr int kAttnKW = 16;                  // keys per warp
+constexpr int kAttnWarpsT = kAttnRows / kAttnKW;  // all six compute warps split the keys
+static_assert(kAttnWarpsT * 32 == kComputeThreads, "every compute warp takes a key block");
 
 template <int HD>
 __device__ __forceinline__ void attn16_stage(const __half* __restrict__ qkv, __half* base, int T, int d, int b, int h,
@@ -346,20 +347,21 @@ __device__ __forceinline__ void attn16_stage(const __half* __restrict__ qkv, __h
   }
 }
 
-// Warp w: scores of the 16 rows against keys [32w, 32w+32), their row max m
+// Warp w: scores of the 16 rows against keys [16w, 16w+16), their row max m
 // and sum l of exp(s - m), and O_w = exp(S - m) V_w (P split f16 hi + lo).
-// Results go to shared memory over the (no longer needed) Q/K rows:
-// float O[3][16][HD], then float ml[3][16][2].
+// Results go to shared memory over the staging rows, which every warp is done
+// with by then: float O[6][16][HD], then float ml[6][16][2].
 template <int HD>
 __device__ __forceinline__ void attn16_keys(__half* base, int T, int w, int lane) {
   constexpr int LD = HD + 8;
   const __half* Qs = base;
   const __half* Ks = base + 16 * LD;
   const __half* Vs = base + (16 + kAttnRows) * LD;
+  constexpr int NJ = kAttnKW / 8;  // 8-key score tiles per warp
   const int g = lane >> 2, t4 = lane & 3;
-  float s[4][4];
+  float s[NJ][4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+  for (int j = 0; j < NJ; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
 #pragma unroll
   for (int kk = 0; kk < HD; kk += 16) {
     uint32_t a[4];
@@ -368,7 +370,7 @@ __device__ __forceinline__ void attn16_keys(__half* base, int T, int w, int lane
       ldsm_x4(a, Qs + ((i & 1) * 8 + (lane & 7)) * LD + kk + (i >> 1) * 8);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < NJ; ++j) {
       uint32_t bb[2];
       ldsm_x2(bb, Ks + (kAttnKW * w + 8 * j + (lane & 7)) * LD + kk + ((lane >> 3) & 1) * 8);
       mma16816(s[j], a, bb[0], bb[1]);
@@ -377,7 +379,7 @@ __device__ __forceinline__ void attn16_keys(__half* base, int T, int w, int lane
   const float scale = 1.0f / sqrtf((float)HD);
   float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
+  for (int j = 0; j < NJ; ++j)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const bool valid = kAttnKW * w + 8 * j + 2 * t4 + e < T;
@@ -393,7 +395,7 @@ __device__ __forceinline__ void attn16_keys(__half* base, int T, int w, int lane
   }
   float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
+  for (int j = 0; j < NJ; ++j)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       s[j][e] = m0 == -INFINITY ? 0.f : expf(s[j][e] - m0);
@@ -450,7 +452,7 @@ __device__ __forceinline__ void attn16_keys(__half* base, int T, int w, int lane
   }
 }
 
-// Combine the 3 key blocks and store rows [q0, q0+16) of out f16 [B*T][d].
+// Combine the key blocks and store rows [q0, q0+16) of out f16 [B*T][d].
 template <int HD>
 __device__ __forceinline__ void attn16_combine(const __half* base, __half* __restrict__ out, int T, int d, int b, int h,
                                                int q0, int tid, int nthr) {
@@ -478,7 +480,13 @@ __device__ __forceinline__ void attn16_combine(const __half* base, __half* __res
   }
 }
 
-size_t attn16_smem_bytes(int hd) { return (size_t)(16 + 2 * kAttnRows) * (hd + 8) * 2; }
+// staging (Q 16 rows, K and V 96 rows, row stride hd + 8 halves), later
+// reused for the per-warp partial outputs and row statistics
+size_t attn16_smem_bytes(int hd) {
+  const size_t stage = (size_t)(16 + 2 * kAttnRows) * (hd + 8) * 2;
+  const size_t part = (size_t)kAttnWarpsT * 16 * hd * 4 + (size_t)kAttnWarpsT * 32 * 4;
+  return stage > part ? stage : part;
+}
 
 template <int HD, int NV>
 __global__ void __launch_bounds__(kTrThreads, 1)
@@ -611,10 +619,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             attn16_stage<HD>(a.qkv, attn, a.T, a.d, b, h, 16 * qb, ct, kComputeThreads);
             cp_async_wait_all();
             named_sync(kBarCompute, kComputeThreads);
-            if (warp < 2 + kAttnWarpsT)
-              attn16_keys<HD>(attn, a.T, warp - 2, lane);
-            else
-              named_sync(kBarCompute, kComputeThreads);  // pairs with the one inside attn16_keys
+            attn16_keys<HD>(attn, a.T, warp - 2, lane);
             named_sync(kBarCompute, kComputeThreads);
             attn16_combine<HD>(attn, a.att, a.T, a.d, b, h, 16 * qb, ct, kComputeThreads);
             fence_proxy_async_global();  // the attention rows are read by TMA
