@@ -98,6 +98,21 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 }
 __device__ __forceinline__ bool dev_error_set() { return *reinterpret_cast<volatile int*>(&g_cn_dev_error) != 0; }
 
+// Phase-trace instrumentation, compiled only with -DCN_TRUNK_TRACE (a
+// profiling build): %globaltimer stamps per (layer, phase, CTA, slot).
+#ifdef CN_TRUNK_TRACE
+__device__ unsigned long long* g_trunk_trace = nullptr;
+#define CN_TR(l, ph, k)                                                                                   \
+  do {                                                                                                   \
+    if (g_trunk_trace)                                                                                   \
+      g_trunk_trace[((((size_t)(l)) * 8 + (ph)) * gridDim.x + blockIdx.x) * 8 + (k)] = global_ns();       \
+  } while (0)
+#else
+#define CN_TR(l, ph, k) \
+  do {                  \
+  } while (0)
+#endif
+
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
@@ -268,7 +283,7 @@ __device__ __forceinline__ void trunk_reduce(const TrunkArgs& a, const float* sl
 template <int NV>
 __device__ __forceinline__ bool trunk_row(const TrunkArgs& a, int src, int sl, const unsigned* src_done,
                                           unsigned target, __half* y, int r, int q, int lane, volatile int* flags,
-                                          float (*lnpart)[2]) {
+                                          float (*lnpart)[2], int trl = 0, int trph = 0) {
   constexpr int d = NV * 512;
   float* xr = a.x + (size_t)r * d + q * (d / 4) + 4 * lane;
   float4 v[NV];
@@ -281,7 +296,10 @@ __device__ __forceinline__ bool trunk_row(const TrunkArgs& a, int src, int sl, c
     const float* bias = a.bias[src] + (size_t)sl * a.bias_lstride + q * (d / 4) + 4 * lane;
 #pragma unroll
     for (int i = 0; i < NV; ++i) b[i] = __ldg(reinterpret_cast<const float4*>(bias + 128 * i));
-    if (threadIdx.x == 128) flags[2] = spin_until(src_done, target, 18, ld_acquire_u32);
+    if (threadIdx.x == 128) {
+      flags[2] = spin_until(src_done, target, 18, ld_acquire_u32);
+      CN_TR(trl, trph, 1);
+    }
     named_sync(kBarEpi, 128);
     live = flags[2] != 0;
     if (live) {
@@ -596,16 +614,21 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           }
           if (warp >= 4)
             for (int r = blockIdx.x; r < a.M; r += gridDim.x) {
-              trunk_row<NV>(a, src, sl, sd, tgt, first ? a.h : a.h2, r, warp & 3, lane, flags, lnpart);
+              if (threadIdx.x == 128) CN_TR(l, ph, 0);
+              trunk_row<NV>(a, src, sl, sd, tgt, first ? a.h : a.h2, r, warp & 3, lane, flags, lnpart, l, ph);
               fence_proxy_async_global();  // the normalised rows are read by TMA
               named_sync(kBarEpi, 128);
-              if (threadIdx.x == 128) red_release_add(dep + (first ? kDepLn1 : kDepLn2), 1u);
+              if (threadIdx.x == 128) {
+                red_release_add(dep + (first ? kDepLn1 : kDepLn2), 1u);
+                CN_TR(l, ph, 2);
+              }
             }
         } else if (ph == 2) {
           // ---------------- attention, one (clip, head, 16 query rows) per CTA
           for (int uu = blockIdx.x; uu < att_units; uu += gridDim.x) {
             const int qb = uu % QB, h = (uu / QB) % a.heads, b = uu / (QB * a.heads);
             if (threadIdx.x == kComputeT0) {
+              CN_TR(l, ph, 0);
               // q, k and v of head h (a 128-feature QKV tile holds 128 / HD heads)
               const unsigned tgt = (unsigned)a.S[TG_QKV] * ep1;
               bool met = spin_until(dep + kDepQkv + (h * HD) / 128, tgt, 19, ld_acquire_u32);
@@ -613,23 +636,29 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               met = met && spin_until(dep + kDepQkv + (2 * a.d + h * HD) / 128, tgt, 19, ld_acquire_u32);
               fence_acq_rel_gpu();
               flags[2] = met;
+              CN_TR(l, ph, 1);
             }
             named_sync(kBarCompute, kComputeThreads);
             if (flags[2] == 0) break;  // uniform: read after the barrier
             attn16_stage<HD>(a.qkv, attn, a.T, a.d, b, h, 16 * qb, ct, kComputeThreads);
             cp_async_wait_all();
             named_sync(kBarCompute, kComputeThreads);
+            if (threadIdx.x == kComputeT0) CN_TR(l, ph, 2);
             attn16_keys<HD>(attn, a.T, warp - 2, lane);
             named_sync(kBarCompute, kComputeThreads);
             attn16_combine<HD>(attn, a.att, a.T, a.d, b, h, 16 * qb, ct, kComputeThreads);
             fence_proxy_async_global();  // the attention rows are read by TMA
             named_sync(kBarCompute, kComputeThreads);
-            if (threadIdx.x == kComputeT0) red_release_add(dep + kDepAtt + h, 1u);
+            if (threadIdx.x == kComputeT0) {
+              red_release_add(dep + kDepAtt + h, 1u);
+              CN_TR(l, ph, 3);
+            }
           }
         } else {
           // ---------------- GEMM slot
           const int gi = ph == 1 ? TG_QKV : (ph == 3 ? TG_O : (ph == 5 ? TG_FC1 : TG_FC2));
           if ((int)blockIdx.x < a.units[gi]) {
+            if (threadIdx.x == kComputeT0) CN_TR(l, ph, 0);
             int nt, s, kb0, kb1;
             unit_range(a, gi, blockIdx.x, &nt, &s, &kb0, &kb1);
             const int nkb = kb1 - kb0;
@@ -652,6 +681,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                 bool met = true;
                 if (gi == TG_QKV || gi == TG_FC1)
                   met = spin_until(dep + (gi == TG_QKV ? kDepLn1 : kDepLn2), (unsigned)M * ep1, 20, ld_acquire_u32);
+                if (warp == 2) CN_TR(l, ph, 1);
                 for (int i = 0; i < nkb && met; i += kKbPerStage, ++gx) {
                   if ((int)(gx & 1) != warp - 2) continue;
                   if (gi == TG_O || gi == TG_FC2) {
@@ -702,6 +732,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               const int n = nt * 128 + e;
               const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
               const bool have = mbar_wait(done, ndone & 1, 15);
+              if (threadIdx.x == 128) CN_TR(l, ph, 2);
               tc_fence_after();
               if (S == 1 && !rowred) {
                 const float bv = a.bias[gi][(size_t)l * a.bias_lstride + n];
@@ -739,7 +770,10 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                 // the barrier orders every epilogue thread's stores before the
                 // release add (TMA readers fence their loads)
                 if (rowred) {
-                  if (e == 0) red_release_add(dep + (gi == TG_O ? kDepOp : kDepFc2p), 1u);
+                  if (e == 0) {
+                    red_release_add(dep + (gi == TG_O ? kDepOp : kDepFc2p), 1u);
+                    CN_TR(l, ph, 3);
+                  }
                 } else if (e == 0) {
                   unsigned* ctr = a.tile_ctr + ((size_t)l * 4 + gi) * kMaxTiles + nt;
                   red_release_add(ctr, 1u);
@@ -774,7 +808,10 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               fence_proxy_async_global();  // outputs read by cp.async (qkv, attention) and TMA (u, fc2)
               named_sync(kBarCompute, kComputeThreads);
               // feature tile nt gained one unit
-              if (threadIdx.x == kComputeT0) red_release_add(dep + (gi == TG_QKV ? kDepQkv : kDepFc1) + nt, 1u);
+              if (threadIdx.x == kComputeT0) {
+                red_release_add(dep + (gi == TG_QKV ? kDepQkv : kDepFc1) + nt, 1u);
+                CN_TR(l, ph, 3);
+              }
             }
             ++ndone;
           }
@@ -1092,6 +1129,15 @@ bool trunk_set_tail(TrunkPlan* tp, const void* const w[3], const float* const b[
   a.out_hid = out_hid;
   return true;
 }
+
+#ifdef CN_TRUNK_TRACE
+// Profiling builds only: point the phase trace at a device buffer of
+// layers x 8 x grid x 8 u64 (null turns it off).
+extern "C" int cn_trunk_trace_set(void* dev_buf) {
+  unsigned long long* p = static_cast<unsigned long long*>(dev_buf);
+  return (int)cudaMemcpyToSymbol(g_trunk_trace, &p, sizeof(p));
+}
+#endif
 
 int trunk_launch(const TrunkPlan& tp, cudaStream_t s) {
   TrunkFn fn = trunk_kernel(tp.hd, tp.a.d);
