@@ -102,6 +102,12 @@ __device__ __forceinline__ bool dev_error_set() { return *reinterpret_cast<volat
 // profiling build): %globaltimer stamps per (layer, phase, CTA, slot).
 #ifdef CN_TRUNK_TRACE
 __device__ unsigned long long* g_trunk_trace = nullptr;
+__device__ unsigned long long* g_trunk_strace = nullptr;  // [layer][4 slots][16 stages][grid][2]
+#define CN_TRS(l, gi, stg, k)                                                                                 \
+  do {                                                                                                       \
+    if (g_trunk_strace && (stg) < 16)                                                                        \
+      g_trunk_strace[((((size_t)(l) * 4 + (gi)) * 16 + (stg)) * gridDim.x + blockIdx.x) * 2 + (k)] = global_ns(); \
+  } while (0)
 #define CN_TR(l, ph, k)                                                                                   \
   do {                                                                                                   \
     if (g_trunk_trace)                                                                                   \
@@ -110,6 +116,9 @@ __device__ unsigned long long* g_trunk_trace = nullptr;
 #else
 #define CN_TR(l, ph, k) \
   do {                  \
+  } while (0)
+#define CN_TRS(l, gi, stg, k) \
+  do {                        \
   } while (0)
 #endif
 
@@ -712,7 +721,10 @@ __global__ void __launch_bounds__(kTrThreads, 1)
               for (int i = 0; i < nkb; i += kKbPerStage, ++gm) {
                 const int st = (int)(gm % ST);
                 const uint32_t par = (gm / ST) & 1;
-                if (!mbar_wait(&fullW[st], par, 13) || !mbar_wait(&fullX[st], par, 1)) break;
+                if (!mbar_wait(&fullW[st], par, 13)) break;
+                CN_TRS(l, gi, i / kKbPerStage, 0);
+                if (!mbar_wait(&fullX[st], par, 1)) break;
+                CN_TRS(l, gi, i / kKbPerStage, 1);
                 tc_fence_after();
                 const uint32_t wa = smem_u32(smem + st * a.stage_bytes);
                 const uint32_t xa = wa + kWStageBytes;
@@ -1136,6 +1148,11 @@ bool trunk_set_tail(TrunkPlan* tp, const void* const w[3], const float* const b[
 extern "C" int cn_trunk_trace_set(void* dev_buf) {
   unsigned long long* p = static_cast<unsigned long long*>(dev_buf);
   return (int)cudaMemcpyToSymbol(g_trunk_trace, &p, sizeof(p));
+}
+// [layers][4][16][grid][2] u64: per GEMM stage, when its weight and its activation tiles had landed
+extern "C" int cn_trunk_strace_set(void* dev_buf) {
+  unsigned long long* p = static_cast<unsigned long long*>(dev_buf);
+  return (int)cudaMemcpyToSymbol(g_trunk_strace, &p, sizeof(p));
 }
 #endif
 
