@@ -102,11 +102,11 @@ __device__ __forceinline__ bool dev_error_set() { return *reinterpret_cast<volat
 // profiling build): %globaltimer stamps per (layer, phase, CTA, slot).
 #ifdef CN_TRUNK_TRACE
 __device__ unsigned long long* g_trunk_trace = nullptr;
-__device__ unsigned long long* g_trunk_strace = nullptr;  // [layer][4 slots][16 stages][grid][2]
+__device__ unsigned long long* g_trunk_strace = nullptr;  // [layer][4 slots][16 stages][grid][8]
 #define CN_TRS(l, gi, stg, k)                                                                                 \
   do {                                                                                                       \
     if (g_trunk_strace && (stg) < 16)                                                                        \
-      g_trunk_strace[((((size_t)(l) * 4 + (gi)) * 16 + (stg)) * gridDim.x + blockIdx.x) * 2 + (k)] = global_ns(); \
+      g_trunk_strace[((((size_t)(l) * 4 + (gi)) * 16 + (stg)) * gridDim.x + blockIdx.x) * 8 + (k)] = global_ns(); \
   } while (0)
 #define CN_TR(l, ph, k)                                                                                   \
   do {                                                                                                   \
@@ -579,6 +579,11 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           ok = false;
           break;
         }
+        {
+          int nt_, s_, kb0_, kb1_;
+          unit_range(a, cur.gi, blockIdx.x, &nt_, &s_, &kb0_, &kb1_);
+          CN_TRS(cur.l, cur.gi, (cur.kb - kb0_) / kKbPerStage, 3);
+        }
         mbar_arrive_expect_tx(&fullW[st], kWStageBytes);
         tma_load_4d_hint(smem + st * a.stage_bytes, &maps.w[cur.gi], &fullW[st], 0, cur.nt * 128, cur.kb, cur.l, wpol);
         last = g + 1;
@@ -708,6 +713,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                   const int st = (int)(gx % ST);
                   const uint32_t par = (gx / ST) & 1;
                   if (!mbar_wait(&empty[st], par ^ 1, 12)) break;
+                  CN_TRS(l, gi, i / kKbPerStage, 4);
                   mbar_arrive_expect_tx(&fullX[st], (uint32_t)(kKbPerStage * a.x_bytes));
                   tma_load_3d(smem + st * a.stage_bytes + kWStageBytes, &maps.x[gi], &fullX[st], 0, 0, kb0 + i);
                   x_last = gx + 1;
@@ -735,6 +741,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                                umma_desc_sw128(xa + h * a.x_bytes + k * 32, 16, 1024), idesc,
                                (i > 0 || h > 0 || k > 0) ? 1u : 0u);
                 tc_commit(&empty[st]);
+                CN_TRS(l, gi, i / kKbPerStage, 2);
               }
               tc_commit(done);
             }
@@ -1149,7 +1156,8 @@ extern "C" int cn_trunk_trace_set(void* dev_buf) {
   unsigned long long* p = static_cast<unsigned long long*>(dev_buf);
   return (int)cudaMemcpyToSymbol(g_trunk_trace, &p, sizeof(p));
 }
-// [layers][4][16][grid][2] u64: per GEMM stage, when its weight and its activation tiles had landed
+// [layers][4][16][grid][8] u64 per GEMM stage: 0 weight tile landed, 1 activation tile landed (both as seen
+// by the MMA thread), 2 MMAs issued, 3 weight load issued, 4 activation load issued
 extern "C" int cn_trunk_strace_set(void* dev_buf) {
   unsigned long long* p = static_cast<unsigned long long*>(dev_buf);
   return (int)cudaMemcpyToSymbol(g_trunk_strace, &p, sizeof(p));
