@@ -20,6 +20,7 @@
 #include "cn_common.cuh"
 #include "cn_gemm.cuh"
 #include "cn_ops.cuh"
+#include "cn_stem.cuh"
 #include "cn_trunk.cuh"
 
 namespace cn {
@@ -158,6 +159,12 @@ struct cn_engine {
   __half* h2 = nullptr;  // LN2 output of the persistent trunk
   uint8_t* tctr = nullptr;
   size_t tctr_bytes = 0;
+  // persistent conv stem (single-clip frames): split-K partials + counters
+  bool use_stem = false;
+  StemPlan stem;
+  float* spart = nullptr;
+  uint8_t* sctr = nullptr;
+  long long spart_floats = 0;
   std::vector<Step> steps;
   std::vector<GemmPlan> plans;
   // side branch of the frame (steps that depend only on the queues, not on the
@@ -246,6 +253,162 @@ static size_t cam_stride_bytes(cn_engine* e, const std::string& cam0name) {
   return (size_t)((uint8_t*)wptr(e, other) - (uint8_t*)wptr(e, cam0name));
 }
 
+// The conv stem, the cond embedding and the token embeddings of a single-clip
+// frame as the phases of one persistent launch (cn_stem.cu).  Phase order:
+// stage 0 (3x3 + fused 1x1), cond, temporal tokens, stage 1 (3x3 + fused 1x1),
+// then stages 2..4 as separate 3x3 and 1x1 phases, then the visual tokens.
+// Returns 0, or -1 if a shape is not covered.
+static int stem_build(cn_engine* e, StemPlan* sp) {
+  const ModelDims& m = e->m;
+  const int B = e->B;
+  stem_plan_begin(sp, e->nsm);
+  auto blank = [] {
+    StemSpec s;
+    memset(&s, 0, sizeof(s));
+    s.dep0 = s.dep1 = -1;
+    return s;
+  };
+  int prev = -1, ph_cond = -1;
+  int cin = 12;
+  for (int st = 0; st < 5; ++st) {
+    const std::string pre = "cam0.s" + std::to_string(st);
+    const int Ho = 64 >> st, Wo = 128 >> st, C = m.stem[st];
+    const int Mg = B * Ho * Wo;
+    StemSpec s = blank();
+    s.G = 2;
+    s.Mg = Mg;
+    s.N = C;
+    if (st == 0) {
+      s.akind = SA_ROWS;
+      s.A = e->a0;
+      s.K = kK0Pad;
+      s.lda = kK0Pad;
+      s.a_gs = (long long)B * 8192 * kK0Pad;
+    } else {
+      s.akind = SA_GATHER;
+      s.A = e->act[st - 1];
+      s.K = 9 * cin;
+      s.Hin = 2 * Ho;
+      s.Win = 2 * Wo;
+      s.Cin = cin;
+      s.a_gs = (long long)B * s.Hin * s.Win * cin;
+    }
+    s.W = wptr(e, pre + ".conv3.w");
+    s.w_gs = (long long)cam_stride_bytes(e, pre + ".conv3.w");
+    s.epi = SE_RELU_F16;
+    s.out = e->y3[st];
+    s.ldo = C;
+    s.o_gs = (long long)Mg * C;
+    s.bias = (const float*)wptr(e, pre + ".conv3.b");
+    s.b_gs = (long long)cam_stride_bytes(e, pre + ".conv3.b") / 4;
+    const bool fuse = st <= 1;
+    if (fuse) {
+      s.W1 = wptr(e, pre + ".conv1.w");
+      s.w1_gs = (long long)cam_stride_bytes(e, pre + ".conv1.w");
+      s.out1 = e->act[st];
+      s.ldo1 = C;
+      s.o1_gs = (long long)Mg * C;
+      s.bias1 = (const float*)wptr(e, pre + ".conv1.b");
+      s.b1_gs = (long long)cam_stride_bytes(e, pre + ".conv1.b") / 4;
+    }
+    s.dep0 = prev;
+    const int p3 = stem_add(sp, s);
+    if (p3 < 0) return -1;
+    prev = p3;
+    if (!fuse) {
+      StemSpec c = blank();
+      c.G = 2;
+      c.Mg = Mg;
+      c.N = C;
+      c.K = C;
+      c.akind = SA_ROWS;
+      c.A = e->y3[st];
+      c.lda = C;
+      c.a_gs = (long long)Mg * C;
+      c.W = wptr(e, pre + ".conv1.w");
+      c.w_gs = (long long)cam_stride_bytes(e, pre + ".conv1.w");
+      c.epi = SE_RELU_F16;
+      c.out = e->act[st];
+      c.ldo = C;
+      c.o_gs = (long long)Mg * C;
+      c.bias = (const float*)wptr(e, pre + ".conv1.b");
+      c.b_gs = (long long)cam_stride_bytes(e, pre + ".conv1.b") / 4;
+      c.dep0 = p3;
+      if ((prev = stem_add(sp, c)) < 0) return -1;
+    }
+    if (st == 0) {
+      // cond embedding (f32, read by both token phases) and the temporal tokens:
+      // they read only what gather0 wrote
+      StemSpec c = blank();
+      c.G = 1;
+      c.Mg = B;
+      c.N = m.d;
+      c.K = kCondPad;
+      c.akind = SA_ROWS;
+      c.A = e->cond16;
+      c.lda = kCondPad;
+      c.W = wptr(e, "cond.w");
+      c.epi = SE_F32;
+      c.out = e->condv;
+      c.ldo = m.d;
+      c.bias = (const float*)wptr(e, "cond.b");
+      if ((ph_cond = stem_add(sp, c)) < 0) return -1;
+      StemSpec t = blank();
+      t.G = 1;
+      t.Mg = B * kNTemp;
+      t.N = m.d;
+      t.K = kFeat;
+      t.akind = SA_ROWS;
+      t.A = e->feat16;
+      t.lda = kFeat;
+      t.W = wptr(e, "temp.w");
+      t.epi = SE_TOKENS;
+      t.out = e->x;
+      t.ldo = m.d;
+      t.bias = (const float*)wptr(e, "temp.b");
+      t.pos = (const float*)wptr(e, "pos");
+      t.cond = e->condv;
+      t.cond_ld = m.d;
+      t.rows_per_clip = kNTemp;
+      t.tok_base = kNVis;
+      t.tok_gstride = 0;
+      t.T = kT;
+      t.dep0 = ph_cond;
+      if (stem_add(sp, t) < 0) return -1;
+    }
+    cin = C;
+  }
+  // visual token embeddings into rows [0, 64) of each clip of x
+  StemSpec v = blank();
+  const int C4 = m.stem[4];
+  v.G = 2;
+  v.Mg = B * kNVisCam;
+  v.N = m.d;
+  v.K = C4;
+  v.akind = SA_ROWS;
+  v.A = e->act[4];
+  v.lda = C4;
+  v.a_gs = (long long)B * kNVisCam * C4;
+  v.W = wptr(e, "cam0.vis.w");
+  v.w_gs = (long long)cam_stride_bytes(e, "cam0.vis.w");
+  v.epi = SE_TOKENS;
+  v.out = e->x;
+  v.ldo = m.d;
+  v.bias = (const float*)wptr(e, "cam0.vis.b");
+  v.b_gs = (long long)cam_stride_bytes(e, "cam0.vis.b") / 4;
+  v.pos = (const float*)wptr(e, "pos");
+  v.cond = e->condv;
+  v.cond_ld = m.d;
+  v.rows_per_clip = kNVisCam;
+  v.tok_base = 0;
+  v.tok_gstride = kNVisCam;
+  v.T = kT;
+  v.dep0 = prev;
+  v.dep1 = ph_cond;
+  if (stem_add(sp, v) < 0) return -1;
+  return 0;
+}
+
 static int layout_acts(cn_engine* e) {
   const int B = e->B;
   const ModelDims& m = e->m;
@@ -286,6 +449,18 @@ static int layout_acts(cn_engine* e) {
     want((void**)&e->h2, R * m.d * 2);
     e->tctr_bytes = trunk_counter_bytes(m.layers);
     want((void**)&e->tctr, e->tctr_bytes);
+  }
+  if (e->use_stem) {
+    // size the partials with a plan over the (not yet placed) activations
+    StemPlan* dry = new StemPlan;
+    if (stem_build(e, dry) == 0) {
+      e->spart_floats = dry->part_floats;
+      want((void**)&e->spart, (size_t)e->spart_floats * 4 + 16);
+      want((void**)&e->sctr, stem_counter_bytes());
+    } else {
+      e->use_stem = false;  // shapes the persistent stem does not cover: per-layer stem kernels
+    }
+    delete dry;
   }
   for (auto& r : req) off += align256(r.second);
   e->abytes = off;
@@ -357,106 +532,114 @@ static int build_plan(cn_engine* e) {
                         },
                         kinfo("border_gather0", dim3(64, 2 * B + 1), dim3(128), dim3(1, 1, 1), 0)});
   }
-  // Side branch: the cond embedding and the temporal tokens read only what
-  // gather0 wrote, so they run beside the conv stem instead of after it.
-  {
-    GemmParams ep;
-    memset(&ep, 0, sizeof(ep));
-    ep.epi = EPI_F32_OUT;
-    ep.out = e->condv;
-    ep.ldo = m.d;
-    ep.bias = (const float*)wptr(e, "cond.b");
-    CN_TRY(add_gemm(e, "cond", e->cond16, kCondPad, 0, wptr(e, "cond.w"), kCondPad, 0, B, m.d, kCondPad, 1, ep));
-    e->steps.back().side = true;
-    e->plans.back().pdl = false;  // first kernel of the branch: its dependency is the fork event
-  }
-  {
-    // temporal token embeddings into rows [kNVis, kT) of each clip of x
-    GemmParams ep;
-    memset(&ep, 0, sizeof(ep));
-    ep.epi = EPI_TOKENS;
-    ep.out = e->x;
-    ep.ldo = m.d;
-    ep.bias = (const float*)wptr(e, "temp.b");
-    ep.bias_gstride = 0;
-    ep.pos = (const float*)wptr(e, "pos");
-    ep.cond = e->condv;
-    ep.cond_ld = m.d;
-    ep.rows_per_clip = kNTemp;
-    ep.tok_base = kNVis;
-    ep.tok_gstride = 0;
-    ep.T = kT;
-    CN_TRY(add_gemm(e, "temp_tokens", e->feat16, kFeat, 0, wptr(e, "temp.w"), kFeat, 0, B * kNTemp, m.d, kFeat, 1,
-                    ep));
-    e->steps.back().side = true;
-  }
-  // conv stem, both cameras as one grouped GEMM per layer
-  int cin = 12;
-  for (int s = 0; s < 5; ++s) {
-    const int Pp = (64 >> s) * (128 >> s);
-    const int C = m.stem[s];
-    const int Ho = 64 >> s, Wo = 128 >> s;
-    const __half* A;
-    int K;
-    if (s == 0) {
-      A = e->a0;
-      K = kK0Pad;
-    } else {
-      K = 9 * cin;
-      const __half* src = e->act[s - 1];
-      __half* dst = e->gat[s];
-      const int Hin = 2 * Ho, Win = 2 * Wo, Ci = cin;
-      const long long total = 2LL * B * Ho * Wo * 9 * (Ci / 8);
-      char nm[64];
-      snprintf(nm, sizeof(nm), "border_gather_s2:s%d", s);
-      e->steps.push_back({nm, [src, dst, B, Hin, Win, Ci](cudaStream_t st) {
-                            return launch_gather_s2(src, 2, B, Hin, Win, Ci, dst, st, true);
-                          },
-                          kinfo(nm, dim3((unsigned)std::min<long long>((total + 255) / 256, 1LL << 20)), dim3(256),
-                                dim3(1, 1, 1), 0)});
-      A = dst;
-    }
-    const std::string pre = "cam0.s" + std::to_string(s);
-    const long long M = (long long)B * Pp;
+  if (e->use_stem) {
+    // conv stem, cond embedding and token embeddings: one persistent launch
+    if (stem_build(e, &e->stem) != 0) return CN_ERR_ARG;
+    CN_TRY(stem_plan_end(&e->stem, e->spart, e->sctr));
+    e->steps.push_back({"stem", [e](cudaStream_t s) { return stem_launch(e->stem, s); },
+                        kinfo("conv_stem", dim3(e->stem.grid), dim3(256), dim3(1, 1, 1), e->stem.smem)});
+  } else {
+    // Side branch: the cond embedding and the temporal tokens read only what
+    // gather0 wrote, so they run beside the conv stem instead of after it.
     {
-      const void* W = wptr(e, pre + ".conv3.w");
-      const float* b = (const float*)wptr(e, pre + ".conv3.b");
-      const long long wgs = cam_stride_bytes(e, pre + ".conv3.w") / 2;
-      const long long bgs = cam_stride_bytes(e, pre + ".conv3.b") / 4;
-      GemmParams ep = epi_f16(e->y3[s], C, M * C, b, bgs, ACT_RELU);
-      CN_TRY(add_gemm(e, "s" + std::to_string(s) + ".conv3", A, K, M * K, W, K, wgs, (int)M, C, K, 2, ep));
+      GemmParams ep;
+      memset(&ep, 0, sizeof(ep));
+      ep.epi = EPI_F32_OUT;
+      ep.out = e->condv;
+      ep.ldo = m.d;
+      ep.bias = (const float*)wptr(e, "cond.b");
+      CN_TRY(add_gemm(e, "cond", e->cond16, kCondPad, 0, wptr(e, "cond.w"), kCondPad, 0, B, m.d, kCondPad, 1, ep));
+      e->steps.back().side = true;
+      e->plans.back().pdl = false;  // first kernel of the branch: its dependency is the fork event
     }
     {
-      const void* W = wptr(e, pre + ".conv1.w");
-      const float* b = (const float*)wptr(e, pre + ".conv1.b");
-      const long long wgs = cam_stride_bytes(e, pre + ".conv1.w") / 2;
-      const long long bgs = cam_stride_bytes(e, pre + ".conv1.b") / 4;
-      GemmParams ep = epi_f16(e->act[s], C, M * C, b, bgs, ACT_RELU);
-      CN_TRY(add_gemm(e, "s" + std::to_string(s) + ".conv1", e->y3[s], C, M * C, W, C, wgs, (int)M, C, C, 2, ep));
+      // temporal token embeddings into rows [kNVis, kT) of each clip of x
+      GemmParams ep;
+      memset(&ep, 0, sizeof(ep));
+      ep.epi = EPI_TOKENS;
+      ep.out = e->x;
+      ep.ldo = m.d;
+      ep.bias = (const float*)wptr(e, "temp.b");
+      ep.bias_gstride = 0;
+      ep.pos = (const float*)wptr(e, "pos");
+      ep.cond = e->condv;
+      ep.cond_ld = m.d;
+      ep.rows_per_clip = kNTemp;
+      ep.tok_base = kNVis;
+      ep.tok_gstride = 0;
+      ep.T = kT;
+      CN_TRY(add_gemm(e, "temp_tokens", e->feat16, kFeat, 0, wptr(e, "temp.w"), kFeat, 0, B * kNTemp, m.d, kFeat, 1,
+                      ep));
+      e->steps.back().side = true;
     }
-    cin = C;
-  }
-  // visual token embeddings into the residual stream x [B*88][d]: rows of
-  // the camera tokens; waits for the side branch (cond, temporal tokens)
-  {
-    GemmParams ep;
-    memset(&ep, 0, sizeof(ep));
-    ep.epi = EPI_TOKENS;
-    ep.out = e->x;
-    ep.ldo = m.d;
-    ep.bias = (const float*)wptr(e, "cam0.vis.b");
-    ep.bias_gstride = cam_stride_bytes(e, "cam0.vis.b") / 4;
-    ep.pos = (const float*)wptr(e, "pos");
-    ep.cond = e->condv;
-    ep.cond_ld = m.d;
-    ep.rows_per_clip = kNVisCam;
-    ep.tok_base = 0;
-    ep.tok_gstride = kNVisCam;
-    ep.T = kT;
-    const int C4 = m.stem[4];
-    CN_TRY(add_gemm(e, "vis_tokens", e->act[4], C4, (long long)B * 32 * C4, wptr(e, "cam0.vis.w"), C4,
-                    cam_stride_bytes(e, "cam0.vis.w") / 2, B * 32, m.d, C4, 2, ep));
-    e->steps.back().join = true;
+    // conv stem, both cameras as one grouped GEMM per layer
+    int cin = 12;
+    for (int s = 0; s < 5; ++s) {
+      const int Pp = (64 >> s) * (128 >> s);
+      const int C = m.stem[s];
+      const int Ho = 64 >> s, Wo = 128 >> s;
+      const __half* A;
+      int K;
+      if (s == 0) {
+        A = e->a0;
+        K = kK0Pad;
+      } else {
+        K = 9 * cin;
+        const __half* src = e->act[s - 1];
+        __half* dst = e->gat[s];
+        const int Hin = 2 * Ho, Win = 2 * Wo, Ci = cin;
+        const long long total = 2LL * B * Ho * Wo * 9 * (Ci / 8);
+        char nm[64];
+        snprintf(nm, sizeof(nm), "border_gather_s2:s%d", s);
+        e->steps.push_back({nm, [src, dst, B, Hin, Win, Ci](cudaStream_t st) {
+                              return launch_gather_s2(src, 2, B, Hin, Win, Ci, dst, st, true);
+                            },
+                            kinfo(nm, dim3((unsigned)std::min<long long>((total + 255) / 256, 1LL << 20)), dim3(256),
+                                  dim3(1, 1, 1), 0)});
+        A = dst;
+      }
+      const std::string pre = "cam0.s" + std::to_string(s);
+      const long long M = (long long)B * Pp;
+      {
+        const void* W = wptr(e, pre + ".conv3.w");
+        const float* b = (const float*)wptr(e, pre + ".conv3.b");
+        const long long wgs = cam_stride_bytes(e, pre + ".conv3.w") / 2;
+        const long long bgs = cam_stride_bytes(e, pre + ".conv3.b") / 4;
+        GemmParams ep = epi_f16(e->y3[s], C, M * C, b, bgs, ACT_RELU);
+        CN_TRY(add_gemm(e, "s" + std::to_string(s) + ".conv3", A, K, M * K, W, K, wgs, (int)M, C, K, 2, ep));
+      }
+      {
+        const void* W = wptr(e, pre + ".conv1.w");
+        const float* b = (const float*)wptr(e, pre + ".conv1.b");
+        const long long wgs = cam_stride_bytes(e, pre + ".conv1.w") / 2;
+        const long long bgs = cam_stride_bytes(e, pre + ".conv1.b") / 4;
+        GemmParams ep = epi_f16(e->act[s], C, M * C, b, bgs, ACT_RELU);
+        CN_TRY(add_gemm(e, "s" + std::to_string(s) + ".conv1", e->y3[s], C, M * C, W, C, wgs, (int)M, C, C, 2, ep));
+      }
+      cin = C;
+    }
+    // visual token embeddings into the residual stream x [B*88][d]: rows of
+    // the camera tokens; waits for the side branch (cond, temporal tokens)
+    {
+      GemmParams ep;
+      memset(&ep, 0, sizeof(ep));
+      ep.epi = EPI_TOKENS;
+      ep.out = e->x;
+      ep.ldo = m.d;
+      ep.bias = (const float*)wptr(e, "cam0.vis.b");
+      ep.bias_gstride = cam_stride_bytes(e, "cam0.vis.b") / 4;
+      ep.pos = (const float*)wptr(e, "pos");
+      ep.cond = e->condv;
+      ep.cond_ld = m.d;
+      ep.rows_per_clip = kNVisCam;
+      ep.tok_base = 0;
+      ep.tok_gstride = kNVisCam;
+      ep.T = kT;
+      const int C4 = m.stem[4];
+      CN_TRY(add_gemm(e, "vis_tokens", e->act[4], C4, (long long)B * 32 * C4, wptr(e, "cam0.vis.w"), C4,
+                      cam_stride_bytes(e, "cam0.vis.w") / 2, B * 32, m.d, C4, 2, ep));
+      e->steps.back().join = true;
+    }
   }
   // transformer
   if (e->use_trunk) {
@@ -736,6 +919,9 @@ int cn_engine_create(const cn_config* cfg, cn_engine** out) {
     {
       const char* tv = getenv("CN_TRUNK");
       e->use_trunk = trunk_supported(e->B * kT, e->m.d, e->m.heads) && !(tv && tv[0] == '0');
+      // the conv stem as one persistent kernel as well; CN_STEM=0 selects the per-layer kernels
+      const char* sv = getenv("CN_STEM");
+      e->use_stem = e->use_trunk && e->B == 1 && !(sv && sv[0] == '0');
     }
     layout_weights(e);
     if (cudaMalloc((void**)&e->wblob, e->wbytes) != cudaSuccess) {
@@ -902,6 +1088,7 @@ int cn_reset_state(cn_engine* e) {
   CN_CUDA(cudaMemsetAsync(e->rings.ctr, 0, sizeof(int), e->stream));
   CN_CUDA(cudaMemsetAsync(e->out, 0, (size_t)e->B * kNOut * 4, e->stream));
   if (e->tctr) CN_CUDA(cudaMemsetAsync(e->tctr, 0, e->tctr_bytes, e->stream));
+  if (e->sctr) CN_CUDA(cudaMemsetAsync(e->sctr, 0, stem_counter_bytes(), e->stream));
   CN_CUDA(cudaStreamSynchronize(e->stream));
   return 0;
 }

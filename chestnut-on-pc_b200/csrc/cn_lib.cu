@@ -6,6 +6,7 @@
 #include "cn_ops.cu"
 #include "cn_attn.cu"
 #include "cn_trunk.cu"
+#include "cn_stem.cu"
 #include "cn_decode.cu"
 #include "cn_engine.cu"
 #include "cn_warp.cu"

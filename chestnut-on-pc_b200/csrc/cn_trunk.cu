@@ -724,6 +724,10 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             if (warp == 4 && lane == 0) {
               tc_fence_after();
               const uint32_t idesc = umma_idesc_f16(a.ntok, false);
+              // kernel-parameter fields held in registers: the asm memory
+              // clobbers of the waits and MMAs would otherwise reload them
+              // per instruction
+              const int stage_bytes = a.stage_bytes, x_bytes = a.x_bytes;
               for (int i = 0; i < nkb; i += kKbPerStage, ++gm) {
                 const int st = (int)(gm % ST);
                 const uint32_t par = (gm / ST) & 1;
@@ -732,13 +736,13 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                 if (!mbar_wait(&fullX[st], par, 1)) break;
                 CN_TRS(l, gi, i / kKbPerStage, 1);
                 tc_fence_after();
-                const uint32_t wa = smem_u32(smem + st * a.stage_bytes);
+                const uint32_t wa = smem_u32(smem + st * stage_bytes);
                 const uint32_t xa = wa + kWStageBytes;
                 for (int h = 0; h < kKbPerStage && i + h < nkb; ++h)
 #pragma unroll
                   for (int k = 0; k < 4; ++k)
                     tc_mma_f16(tmem, umma_desc_sw128(wa + h * kWTileBytes + k * 32, 16, 1024),
-                               umma_desc_sw128(xa + h * a.x_bytes + k * 32, 16, 1024), idesc,
+                               umma_desc_sw128(xa + h * x_bytes + k * 32, 16, 1024), idesc,
                                (i > 0 || h > 0 || k > 0) ? 1u : 0u);
                 tc_commit(&empty[st]);
                 CN_TRS(l, gi, i / kKbPerStage, 2);

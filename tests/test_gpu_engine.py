@@ -39,15 +39,18 @@ def params39():
     return omodel.gen_params(spec.CONFIGS["39m"], 3)
 
 
-@pytest.mark.parametrize("trunk", ["persistent", "per-layer"])
-def test_39m_frames_match_oracle_with_hidden_carry(params39, trunk, monkeypatch):
-    # single-clip engines run the transformer as one persistent kernel unless CN_TRUNK=0
-    monkeypatch.setenv("CN_TRUNK", "1" if trunk == "persistent" else "0")
+@pytest.mark.parametrize("mode", ["persistent", "per-layer stem", "per-layer"])
+def test_39m_frames_match_oracle_with_hidden_carry(params39, mode, monkeypatch):
+    # single-clip engines run the conv stem and the transformer as one
+    # persistent kernel each unless CN_STEM=0 / CN_TRUNK=0
+    monkeypatch.setenv("CN_TRUNK", "0" if mode == "per-layer" else "1")
+    monkeypatch.setenv("CN_STEM", "1" if mode == "persistent" else "0")
     rs = np.random.default_rng(0)
     w, pk = frame_inputs(rs, 12)
     eng = Engine("39m", seed=3)
     names = [k["name"] for k in eng.kernel_list()]
-    assert ("transformer_trunk" in names) == (trunk == "persistent")
+    assert ("transformer_trunk" in names) == (mode != "per-layer")
+    assert ("conv_stem" in names) == (mode == "persistent")
     clip = omodel.Clip("39m", 3, params39)
     pg, po = pk[0].copy(), pk[0].copy()
     for f in range(len(w)):
@@ -128,16 +131,22 @@ def test_batched_clips_match_single_clip_engines():
 
 
 def test_kernel_list_describes_the_frame(monkeypatch):
-    # stem 10 + cond/tokens 3 GEMMs; the transformer, the final LayerNorm, the
-    # token mean and the three head products as one persistent launch
+    # the conv stem with the cond and token embeddings as one persistent
+    # launch; the transformer, the final LayerNorm, the token mean and the
+    # three head products as another
     eng = Engine("39m", seed=0)
     ks = eng.kernel_list()
     names = [k["name"] for k in ks]
-    assert names[0] == "queue_push" and names[1] == "border_gather0"
+    assert names == ["queue_push", "border_gather0", "conv_stem", "transformer_trunk"]
+    assert eng.info()["n_kernels"] == len(ks)
+    # per-layer stem: 10 conv GEMMs (4 im2col gathers) + cond / tokens 3 GEMMs
+    monkeypatch.setenv("CN_STEM", "0")
+    names = [k["name"] for k in Engine("39m", seed=0).kernel_list()]
     assert sum(n.startswith("gemm_tc") for n in names) == 10 + 3
+    assert sum(n.startswith("border_gather_s2") for n in names) == 4
     assert names.count("transformer_trunk") == 1
     assert "token_mean_pool" not in names and "layernorm:final" not in names
-    assert eng.info()["n_kernels"] == len(ks)
+    monkeypatch.delenv("CN_STEM")
     # per-layer kernels: 4 GEMMs per layer, then final LN, pool and 3 head GEMMs
     monkeypatch.setenv("CN_TRUNK", "0")
     names = [k["name"] for k in Engine("39m", seed=0).kernel_list()]
@@ -146,17 +155,19 @@ def test_kernel_list_describes_the_frame(monkeypatch):
     assert "token_mean_pool" in names and "layernorm:final" in names
 
 
-def test_persistent_trunk_is_deterministic_and_matches_per_layer_kernels(monkeypatch):
+@pytest.mark.parametrize("cfg", ["39m", "1b"])
+def test_persistent_kernels_are_deterministic_and_match_per_layer_kernels(cfg, monkeypatch):
     rs = np.random.default_rng(8)
     w, pk = frame_inputs(rs, 4)
-    a, b = Engine("39m", seed=5), Engine("39m", seed=5, use_graph=False)
+    a, b = Engine(cfg, seed=5), Engine(cfg, seed=5, use_graph=False)
     monkeypatch.setenv("CN_TRUNK", "0")
-    ref = Engine("39m", seed=5)
+    ref = Engine(cfg, seed=5)
     for f in range(4):
         oa, ob, orf = a.run_frame(w[f], pk[f]), b.run_frame(w[f], pk[f]), ref.run_frame(w[f], pk[f])
         assert np.array_equal(oa, ob), f          # graph replay == eager, run to run identical
         errs = head_errors(oa, orf)
         assert all(ok for _, ok in errs.values()), (f, errs)
+    assert a.run_frame(w[0], pk[0]).shape == (spec.N_OUT,)
 
 
 @pytest.mark.slow
