@@ -255,8 +255,9 @@ static size_t cam_stride_bytes(cn_engine* e, const std::string& cam0name) {
 
 // The conv stem, the cond embedding and the token embeddings of a single-clip
 // frame as the phases of one persistent launch (cn_stem.cu).  Phase order:
-// stage 0 (3x3 + fused 1x1), cond, temporal tokens, stage 1 (3x3 + fused 1x1),
-// then stages 2..4 as separate 3x3 and 1x1 phases, then the visual tokens.
+// stage 0 (3x3 + fused 1x1), cond, temporal tokens, stage 1, then the other
+// stages (the 1x1 fused while the stage has at most 256 channels), then the
+// visual tokens.
 // Returns 0, or -1 if a shape is not covered.
 static int stem_build(cn_engine* e, StemPlan* sp) {
   const ModelDims& m = e->m;
@@ -301,7 +302,7 @@ static int stem_build(cn_engine* e, StemPlan* sp) {
     s.o_gs = (long long)Mg * C;
     s.bias = (const float*)wptr(e, pre + ".conv3.b");
     s.b_gs = (long long)cam_stride_bytes(e, pre + ".conv3.b") / 4;
-    const bool fuse = st <= 1;
+    const bool fuse = C <= 256;  // the 1x1 runs inside the 3x3 unit while a tile's channels fit one MMA
     if (fuse) {
       s.W1 = wptr(e, pre + ".conv1.w");
       s.w1_gs = (long long)cam_stride_bytes(e, pre + ".conv1.w");

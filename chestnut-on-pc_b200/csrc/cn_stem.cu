@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
       // starts only once the epilogue has read out the unit before last.
       uint32_t gw = 0, ga = 0, ny = 0, lu = 0;
       bool ok = true;
-      const uint32_t ring_a = smem_u32(ringA), ring_w = smem_u32(smem), ybase = smem_u32(Y);
+      const uint32_t ring_a = smem_u32(ringA), ring_w = smem_u32(smem);
       for (int p = 0; p < a.nph && ok; ++p) {
         const StemPhase& P = sph[p];
         const int units = P.units, KB1 = P.fuse ? P.KB1 : 0;
@@ -394,10 +394,10 @@ __global__ void __launch_bounds__(kStThreads, 1)
                 break;
               }
               tc_fence_after();
-              const uint32_t ya = ybase + kb * kStABytes, wa = ring_w + sw * kStWBytes + sub * wsub1;
+              const uint32_t ya = ring_a + kb * kStABytes, wa = ring_w + sw * kStWBytes + sub * wsub1;
 #pragma unroll
               for (int k = 0; k < 4; ++k)
-                tc_mma_f16(acc + 128, umma_desc_sw128(ya + 32 * k, 16, 1024), umma_desc_sw128(wa + 32 * k, 16, 1024),
+                tc_mma_f16(acc, umma_desc_sw128(ya + 32 * k, 16, 1024), umma_desc_sw128(wa + 32 * k, 16, 1024),
                            idesc1, (kb > 0 || k > 0) ? 1u : 0u);
               if (++sub == kps1 || kb + 1 == KB1) {
                 tc_commit(&emptyW[sw]);
@@ -599,8 +599,11 @@ __global__ void __launch_bounds__(kStThreads, 1)
             const int nout = fuse ? N : BN;
             const int pitch = nout * 2 + 16;  // staging row stride (bytes)
             if (fuse) {
-              // 3x3 output (ReLU, f16) -> the 1x1 conv's operand in Y (swizzled k-blocks);
-              // columns past N in the last k-block are zeros
+              // 3x3 output (ReLU, f16) -> the 1x1 conv's operand in the
+              // activation ring (idle once the 3x3 MMAs are done; the next
+              // unit's loads wait for this unit's closing verdict), swizzled
+              // k-blocks, columns past N in the last k-block zero.  The 1x1
+              // then accumulates into the same TMEM columns.
               if (live) {
                 for (int c0 = 0; c0 < N; c0 += 16) {
                   uint32_t r[16];
@@ -611,13 +614,13 @@ __global__ void __launch_bounds__(kStThreads, 1)
 #pragma unroll
                   for (int hh = 0; hh < 2; ++hh) {
                     const int c = c0 + 8 * hh, kb = c >> 6, jc = (c & 63) >> 3;
-                    *reinterpret_cast<uint4*>(Y + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
+                    *reinterpret_cast<uint4*>(ringA + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
                         *reinterpret_cast<const uint4*>(h + 8 * hh);
                   }
                 }
                 for (int c = N; c < KB1 * 64; c += 8) {
                   const int kb = c >> 6, jc = (c & 63) >> 3;
-                  *reinterpret_cast<uint4*>(Y + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
+                  *reinterpret_cast<uint4*>(ringA + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
                       make_uint4(0, 0, 0, 0);
                 }
               }
@@ -630,8 +633,9 @@ __global__ void __launch_bounds__(kStThreads, 1)
               if (threadIdx.x == 128) CN_ST(p, 8);
               tc_fence_after();
             }
-            // final accumulator -> staging rows in Y -> coalesced copy-out
-            const uint32_t acc = taddr + (fuse ? 128u : 0u);
+            // final accumulator -> staging rows at the activation ring (and
+            // Y after it: 128 rows x (2 N + 16) bytes) -> coalesced copy-out
+            const uint32_t acc = taddr;  // the fused 1x1 accumulates into the 3x3's columns
             const float* bias = fuse ? sbias + 256 : sbias;
             if (epi == SE_RELU_F16 || fuse) {
               if (live)
@@ -641,7 +645,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
                   tmem_ld_wait();
                   __align__(16) __half h[16];
                   st_relu16(r, bias + c0, h);
-                  uint4* d = reinterpret_cast<uint4*>(Y + row * pitch + c0 * 2);
+                  uint4* d = reinterpret_cast<uint4*>(ringA + row * pitch + c0 * 2);
                   d[0] = reinterpret_cast<const uint4*>(h)[0];
                   d[1] = reinterpret_cast<const uint4*>(h)[1];
                 }
@@ -656,7 +660,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
                 for (int i = threadIdx.x - 128; i < rv * cpr; i += 128) {
                   const int rr = i / cpr, cc = i % cpr;
                   *reinterpret_cast<uint4*>(out + (long long)(U.tm * 128 + rr) * ldo + 8 * cc) =
-                      *reinterpret_cast<const uint4*>(Y + rr * pitch + cc * 16);
+                      *reinterpret_cast<const uint4*>(ringA + rr * pitch + cc * 16);
                 }
             } else {
               // f32 / token tiles (at most 32 rows): the warps holding valid
@@ -887,8 +891,8 @@ int stem_add(StemPlan* sp, const StemSpec& s) {
   P.S = S;
   const bool ok_shape = s.G >= 1 && s.Mg >= 1 && s.N % 16 == 0 && s.N % P.BN == 0 && P.BN >= 16 && P.BN <= 256 &&
                         s.K % 8 == 0 && (s.akind == SA_ROWS || (s.akind == SA_GATHER && s.Cin % 8 == 0)) &&
-                        (!fuse || (s.N <= 128 && s.epi == SE_RELU_F16)) &&
-                        (S > 1 || fuse || s.epi != SE_RELU_F16 || std::min(128, s.Mg) * (P.BN * 2 + 16) <= kStYBytes) &&
+                        (!fuse || (s.N <= 256 && s.epi == SE_RELU_F16)) &&
+                        (S > 1 || s.epi != SE_RELU_F16 || std::min(128, s.Mg) * ((fuse ? s.N : P.BN) * 2 + 16) <= kStRedBytes) &&
                         (S > 1 || fuse || s.epi == SE_RELU_F16 || P.rows_pad * (P.BN + 4) * 4 <= kStYBytes) &&
                         (s.akind != SA_GATHER || (pow2(s.Hin) && pow2(s.Win) && pow2(s.Cin) && s.Cin >= 8)) &&
                         (S == 1 || (tiles <= kStemMaxTiles && red_bytes(S) <= kStRedBytes)) &&

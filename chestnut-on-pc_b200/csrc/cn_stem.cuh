@@ -39,7 +39,7 @@ struct StemSpec {
   long long cond_ld;
   int rows_per_clip, tok_base, tok_gstride, T;
   // Optional fused 1x1 conv on this GEMM's ReLU output (N x N weights, same
-  // rows): out1 = f16(relu(relu_out . W1^T + bias1)).  N <= 128.
+  // rows): out1 = f16(relu(relu_out . W1^T + bias1)).  N <= 256.
   const void* W1;
   long long w1_gs;
   void* out1;
