@@ -73,6 +73,17 @@ __device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, u
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// TMA tile store from shared memory (no multicast; never at a negative
+// coordinate), and its bulk-group bookkeeping.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Wait until at most n (< 4) copy groups of this thread are in flight.
 __device__ __forceinline__ void cp_async_wait_pending(int n) {
   switch (n) {
@@ -258,6 +269,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
     for (int p = 0; p < a.nph; ++p) {
       tma_prefetch_desc(&maps.w[p]);
       if (a.ph[p].atma) tma_prefetch_desc(&maps.x[p]);
+      if (a.ph[p].S == 1 && (a.ph[p].fuse || a.ph[p].epi == SE_RELU_F16)) tma_prefetch_desc(&maps.o[p]);
       if (a.ph[p].fuse) tma_prefetch_desc(&maps.w1[p]);  // (before the table copy is visible)
     }
   }
@@ -575,7 +587,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
           __syncwarp();
         } else {
           // ---------------- epilogue: TMEM lane quadrant q, one accumulator row per thread
-          const int q = warp & 3, row = 32 * q + lane, m = U.tm * 128 + row;
+          const int q = warp & 3, row = 32 * q + lane;
           const int rv = min(128, Mg - U.tm * 128);  // valid rows of the tile
           const uint32_t taddr = tmem + 256u * (lu & 1) + ((uint32_t)(32 * q) << 16);
           {
@@ -597,7 +609,6 @@ __global__ void __launch_bounds__(kStThreads, 1)
           tc_fence_after();
           if (S == 1) {
             const int nout = fuse ? N : BN;
-            const int pitch = nout * 2 + 16;  // staging row stride (bytes)
             if (fuse) {
               // 3x3 output (ReLU, f16) -> the 1x1 conv's operand in the
               // activation ring (idle once the 3x3 MMAs are done; the next
@@ -633,11 +644,13 @@ __global__ void __launch_bounds__(kStThreads, 1)
               if (threadIdx.x == 128) CN_ST(p, 8);
               tc_fence_after();
             }
-            // final accumulator -> staging rows at the activation ring (and
-            // Y after it: 128 rows x (2 N + 16) bytes) -> coalesced copy-out
+            // final accumulator -> output
             const uint32_t acc = taddr;  // the fused 1x1 accumulates into the 3x3's columns
             const float* bias = fuse ? sbias + 256 : sbias;
             if (epi == SE_RELU_F16 || fuse) {
+              // rows -> the activation ring as swizzled 64-column tiles (the
+              // TMA layout), then one thread stores them with TMA, waits for
+              // the writes and publishes (no copy loop, no proxy fence)
               if (live)
                 for (int c0 = 0; c0 < nout; c0 += 16) {
                   uint32_t r[16];
@@ -645,23 +658,29 @@ __global__ void __launch_bounds__(kStThreads, 1)
                   tmem_ld_wait();
                   __align__(16) __half h[16];
                   st_relu16(r, bias + c0, h);
-                  uint4* d = reinterpret_cast<uint4*>(ringA + row * pitch + c0 * 2);
-                  d[0] = reinterpret_cast<const uint4*>(h)[0];
-                  d[1] = reinterpret_cast<const uint4*>(h)[1];
+#pragma unroll
+                  for (int hh = 0; hh < 2; ++hh) {
+                    const int c = c0 + 8 * hh, kb = c >> 6, jc = (c & 63) >> 3;
+                    *reinterpret_cast<uint4*>(ringA + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
+                        *reinterpret_cast<const uint4*>(h + 8 * hh);
+                  }
                 }
+              fence_proxy_async_smem();
               tc_fence_before();
               named_sync(kStBarEpi, 128);
-              if (threadIdx.x == 128) mbar_arrive(&tfree[lu & 1]);
-              const int cpr = nout / 8;
-              __half* out = reinterpret_cast<__half*>(fuse ? P.out1 : P.out) +
-                            (long long)U.g * (fuse ? P.o1_gs : P.o_gs) + (fuse ? 0 : U.tn * BN);
-              const long long ldo = fuse ? P.ldo1 : P.ldo;
-              if (live)
-                for (int i = threadIdx.x - 128; i < rv * cpr; i += 128) {
-                  const int rr = i / cpr, cc = i % cpr;
-                  *reinterpret_cast<uint4*>(out + (long long)(U.tm * 128 + rr) * ldo + 8 * cc) =
-                      *reinterpret_cast<const uint4*>(ringA + rr * pitch + cc * 16);
+              if (threadIdx.x == 128) {
+                mbar_arrive(&tfree[lu & 1]);
+                if (live) {
+                  const int col0 = fuse ? 0 : U.tn * BN;
+                  for (int kb = 0; kb * 64 < nout; ++kb)
+                    tma_store_3d(&maps.o[p], ringA + kb * kStABytes, col0 + kb * 64, U.tm * 128, U.g);
+                  bulk_commit();
+                  bulk_wait_all();
+                  fence_proxy_async_global();
                 }
+                red_release_add(a.pctr + p, 1u);
+                CN_ST(p, 11);
+              }
             } else {
               // f32 / token tiles (at most 32 rows): the warps holding valid
               // rows stage the accumulators in Y ([row][BN + 4] f32), then all
@@ -703,11 +722,13 @@ __global__ void __launch_bounds__(kStThreads, 1)
                   st_emit8(E, U.g, U.tm * 128 + rr, U.tn * BN + 8 * cg, v, sbias + 8 * cg);
                 }
             }
-            fence_proxy_async_global();  // the next phases read these rows by TMA
-            named_sync(kStBarEpi, 128);
-            if (threadIdx.x == 128) {
-              red_release_add(a.pctr + p, 1u);
-              CN_ST(p, 11);
+            if (epi != SE_RELU_F16 && !fuse) {
+              fence_proxy_async_global();  // the next phases read these rows by TMA
+              named_sync(kStBarEpi, 128);
+              if (threadIdx.x == 128) {
+                red_release_add(a.pctr + p, 1u);
+                CN_ST(p, 11);
+              }
             }
           } else {
             // partial tile [BN][rows_pad] -> global (lane = row: whole 128-byte lines per store)
@@ -892,7 +913,7 @@ int stem_add(StemPlan* sp, const StemSpec& s) {
   const bool ok_shape = s.G >= 1 && s.Mg >= 1 && s.N % 16 == 0 && s.N % P.BN == 0 && P.BN >= 16 && P.BN <= 256 &&
                         s.K % 8 == 0 && (s.akind == SA_ROWS || (s.akind == SA_GATHER && s.Cin % 8 == 0)) &&
                         (!fuse || (s.N <= 256 && s.epi == SE_RELU_F16)) &&
-                        (S > 1 || s.epi != SE_RELU_F16 || std::min(128, s.Mg) * ((fuse ? s.N : P.BN) * 2 + 16) <= kStRedBytes) &&
+                        (S > 1 || s.epi != SE_RELU_F16 || ((fuse ? s.N : P.BN) + 63) / 64 <= kStAStages) &&
                         (S > 1 || fuse || s.epi == SE_RELU_F16 || P.rows_pad * (P.BN + 4) * 4 <= kStYBytes) &&
                         (s.akind != SA_GATHER || (pow2(s.Hin) && pow2(s.Win) && pow2(s.Cin) && s.Cin >= 8)) &&
                         (S == 1 || (tiles <= kStemMaxTiles && red_bytes(S) <= kStRedBytes)) &&
@@ -996,6 +1017,16 @@ int stem_plan_end(StemPlan* sp, float* part, void* counters) {
       const uint32_t box[4] = {64, (uint32_t)(2 * P.Wo), (uint32_t)(2 * rows), 1};
       const uint32_t es[4] = {1, 2, 2, 1};
       if (encode_strided(&sp->maps.x[p], 4, P.A, d, st, box, es)) return -3;
+    }
+    if (P.S == 1 && (P.fuse || P.epi == SE_RELU_F16)) {
+      // f16 output rows (the fused 1x1's for fused phases), 64 x 128 boxes
+      const void* o = P.fuse ? P.out1 : P.out;
+      const long long ldo = P.fuse ? P.ldo1 : P.ldo, ogs = P.fuse ? P.o1_gs : P.o_gs;
+      const uint64_t d[3] = {(uint64_t)P.N, (uint64_t)P.Mg, (uint64_t)P.G};
+      const uint64_t st[2] = {(uint64_t)ldo * 2, (uint64_t)(P.G > 1 ? ogs : (long long)P.Mg * ldo) * 2};
+      const uint32_t box[3] = {64, 128, 1};
+      if (encode(&sp->maps.o[p], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, o, d, st, box, CU_TENSOR_MAP_SWIZZLE_128B))
+        return -3;
     }
     if (P.fuse) {
       const uint64_t d[4] = {64, (uint64_t)P.N, (uint64_t)P.KB1, (uint64_t)P.G};

@@ -89,6 +89,8 @@ struct StemMaps {
   // SA_GATHER: NHWC (Cin, Win, Hin, G x B) with traversal strides (1, 2, 2, 1),
   // box 64 x 2 Wo x 2 R x 1: the R x Wo output pixels of a tile for one tap.
   CUtensorMap x[kStemMaxPhases];
+  // f16 outputs of whole-unit ReLU phases: (N, rows, G), box 64 x 128 x 1
+  CUtensorMap o[kStemMaxPhases];
 };
 
 struct StemArgs {
