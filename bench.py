@@ -173,6 +173,20 @@ def frame_flops(model):
     return 2 * macs
 
 
+def stem_weight_bytes(model):
+    """f16 weight bytes the persistent stem streams per frame: both cameras'
+    conv stages (first conv K padded to 128), the cond embedding (K padded to
+    256), the temporal and visual token embeddings."""
+    stem, d, _, _ = MODEL_DIMS[model]
+    n, cin = 0, None
+    for s, c in enumerate(stem):
+        k = 128 if s == 0 else 9 * cin
+        n += 2 * (c * k + c * c)
+        cin = c
+    n += 2 * d * stem[-1] + 256 * d + 512 * d
+    return 2 * n
+
+
 # ------------------------------------------------------------ kernel-level legs
 def bench_gemm(reps=50, bn=0, splits=0, b_kmajor=0):
     """Config 1: C f32[768x256] += A f16[768x6144] x B f16[6144x256] ([K][N], the
@@ -470,6 +484,17 @@ def run_ours(args, rank, world, local_rank):
         eng.sync()
         kms += eng.timed_class_ms()
     eng.set_timed_class("")
+    # the persistent conv stem (single-clip frames), timed the same way
+    stem_ms = None
+    if any(k["name"] == "conv_stem" for k in eng.kernel_list()):
+        eng.set_timed_class("conv_stem")
+        sms = []
+        for i in range(args.steps):
+            eng.run_frame_device(dW[i % nfr].ptr, dP[i % nfr].ptr)
+            eng.sync()
+            sms += eng.timed_class_ms()
+        eng.set_timed_class("")
+        stem_ms = statistics.median(sms) if sms else None
 
     # ---- e2e through the public run_frame with pinned host buffers
     hw = ctypes.c_void_p()
@@ -569,6 +594,10 @@ def run_ours(args, rank, world, local_rank):
                      "traffic": ncu_traffic(args.model) if trunk else None},
         "frame_roofline": {"bound": "hbm", "weight_bytes": info["weight_bytes"], "floor_ms": floor_ms,
                            "frac": floor_ms / lat[len(lat) // 2]},
+        "stem": ({"kernel": "conv_stem (persistent: 5 conv stages, cond and token embeddings)",
+                  "ms_per_launch_median": stem_ms, "weight_bytes": stem_weight_bytes(args.model),
+                  "note": "a dependency chain of 10 GEMM phases, latency-bound (profiles/stem_1b.md)"}
+                 if stem_ms is not None else None),
         "clocks": clk.summary(),
         "clip_digests": allv[:, 2].tolist(),
     }

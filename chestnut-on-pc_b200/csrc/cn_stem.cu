@@ -3,7 +3,7 @@
 // The conv stem of a frame (compile_modeld.py's vision encoder as restated in
 // the synthetic layer list: per camera five 3x3 / stride-2 convs, each with a
 // 1x1 conv, ReLU) plus the conditioning and token-embedding GEMMs are ~3.6
-// GFLOP over ~40 MB of weights: microseconds of work, but eleven dependent
+// GFLOP over ~42 MB of weights: microseconds of work, but eleven dependent
 // GEMMs.  As separate launches each paid its launch, pipeline fill, an
 // im2col pass through HBM and a split-K cluster exchange (~120 us in all).
 // This kernel runs them as one cooperative launch of one CTA per SM:
