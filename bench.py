@@ -521,7 +521,7 @@ def run_ours(args, rank, world, local_rank):
 
     eng.close()
 
-    # ---- config 5: clip throughput of the 39M model, 8 clips per launch
+    # ---- config 5: clip throughput of the 39M model, a rank's clips batched per launch
     clip = clip_throughput(args, rank, world, dev, dist, barrier) if args.clips > 0 else None
     clk.__exit__()
 
@@ -628,19 +628,22 @@ def run_ours(args, rank, world, local_rank):
 
 
 def clip_throughput(args, rank, world, dev, dist, barrier):
-    """Config 5: this rank's share of the clips, 8 per launch, frames through run_frame."""
+    """Config 5: this rank's share of the clips, `--clip-batch` per launch
+    (default: all of the rank's clips, at most 64), frames through run_frame."""
     import torch
     from chestnut_b200 import Engine, clips
     from chestnut_b200._lib import lib
 
-    B = 8
     mine = clips.assign(args.clips, world, rank)
+    B = args.clip_batch if args.clip_batch > 0 else max(1, min(64, len(mine)))
     eng = Engine("39m", device=dev, batch=B, seed=args.seed)
     stream = torch.cuda.ExternalStream(eng.stream_handle(), device=dev)
     # clip c, frame f reads pool frame (c + f) % 4 with clip-specific desire: a pure
-    # function of (clip, frame), so the gathered results match for any GPU count.
-    # The batches are staged once in pinned host memory, as a camera pipeline
-    # hands the engine its frames.
+    # function of (clip, frame), so the gathered results agree for any GPU count
+    # (bit for bit at equal clips per launch; the batched GEMMs tile by M, so
+    # other batch sizes differ in the f32 summation order only).  The batches
+    # are staged once in pinned host memory, as a camera pipeline hands the
+    # engine its frames.
     rng = np.random.default_rng(77)
     pool = rng.integers(0, 256, (4, 2, 6, 128, 256), dtype=np.uint8)
     groups = clips.batches(mine, B)
@@ -754,6 +757,8 @@ def main():
     ap.add_argument("--latency-frames", type=int, default=1200, help="recurrent frames of the latency_1200 leg")
     ap.add_argument("--clips", type=int, default=64, help="config-5 clips (0 skips the clip-throughput leg)")
     ap.add_argument("--clip-frames", type=int, default=1200, help="frames per clip in the clip-throughput leg")
+    ap.add_argument("--clip-batch", type=int, default=0,
+                    help="clips per launch in the clip-throughput leg (0: all of a rank's clips, at most 64)")
     ap.add_argument("--kernel", choices=["gemm", "reduce", "frame39m", "warp"],
                     help="run one kernel-level leg alone and print its JSON")
     ap.add_argument("--bn", type=int, default=0)
