@@ -612,7 +612,9 @@ def run_ours(args, rank, world, local_rank):
             "workload": f"config 5: {args.clips} synthetic 39M clips x {args.clip_frames} frames, {clip['batch']} clips "
                         f"per graph launch, round-robin over {world} GPU(s), per-clip results gathered once at "
                         "clip end", "value": fps, "unit": "frames/s", "ms": cms, "scaling": "strong",
-            "path": "public run_frame, frames from pinned host memory (H2D + D2H per launch)",
+            "path": "public C ABI (cn_stage_input / cn_run_staged_async / cn_wait_output: frame f+1 uploaded and "
+                    "queued while the host reads frame f), frames and outputs in pinned host memory, H2D + D2H "
+                    "every frame, hidden state carried on the device",
             "gather": clip["gather"],
             "roofline": {"bound": "tensor", "per_launch_floor_ms": per_launch_ms, "frames_per_s_floor": roof_fps,
                          "frac": fps / roof_fps, "flops_per_frame": fl, "weight_bytes": w39, "peak_source": src},
@@ -631,12 +633,14 @@ def clip_throughput(args, rank, world, dev, dist, barrier):
     """Config 5: this rank's share of the clips, `--clip-batch` per launch
     (default: all of the rank's clips, at most 64), frames through run_frame."""
     import torch
-    from chestnut_b200 import Engine, clips
+    from chestnut_b200 import Engine, PinnedArray, clips
     from chestnut_b200._lib import lib
 
     mine = clips.assign(args.clips, world, rank)
     B = args.clip_batch if args.clip_batch > 0 else max(1, min(64, len(mine)))
-    eng = Engine("39m", device=dev, batch=B, seed=args.seed)
+    # the hidden state is carried on the device (bit for bit the host carry), so
+    # the runner queues frame f+1 before it reads frame f's output
+    eng = Engine("39m", device=dev, batch=B, seed=args.seed, carry_hidden=True)
     stream = torch.cuda.ExternalStream(eng.stream_handle(), device=dev)
     # clip c, frame f reads pool frame (c + f) % 4 with clip-specific desire: a pure
     # function of (clip, frame), so the gathered results agree for any GPU count
@@ -668,21 +672,29 @@ def clip_throughput(args, rank, world, dev, dist, barrier):
         return w, pk.copy()
 
     def factory(n):
-        return eng if n == B else Engine("39m", device=dev, batch=n, seed=args.seed)
+        return eng if n == B else Engine("39m", device=dev, batch=n, seed=args.seed, carry_hidden=True)
 
-    clips.run_rank(factory, None, groups[0], 3, B, batch_source)  # warm-up
+    pinned = []
+
+    def alloc(shape, dtype):
+        pinned.append(PinnedArray(shape, dtype))
+        return pinned[-1].array
+
+    clips.run_rank_pipelined(factory, groups[0], 3, B, batch_source, alloc)  # warm-up
     eng.reset()
     barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    res = clips.run_rank(factory, None, mine, args.clip_frames, B, batch_source)
+    res = clips.run_rank_pipelined(factory, mine, args.clip_frames, B, batch_source, alloc)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)
     weight_bytes = eng.info()["weight_bytes"]
     eng.close()
     lib().cn_host_free_pinned(pin)
+    for p in pinned:
+        p.free()
     # the clip-end gather: NCCL driven from C++ (libcncomm.so); the bench's own
     # process group only hands the rendezvous id to every rank
     transport = None

@@ -49,6 +49,10 @@ _SIGS = {
     "cn_engine_create": ([ctypes.POINTER(cn_config), ctypes.POINTER(_vp)], _i),
     "cn_engine_destroy": ([_vp], _i),
     "cn_run_frame": ([_vp, _vp, _vp, _vp], _i),
+    "cn_stage_input": ([_vp, _vp], _i),
+    "cn_run_staged": ([_vp, _vp, _vp], _i),
+    "cn_run_staged_async": ([_vp, _vp, _vp], _i),
+    "cn_wait_output": ([_vp], _i),
     "cn_run_frames": ([_vp, _i, _vp, _vp, _vp], _i),
     "cn_run_frame_device": ([_vp, _vp, _vp], _i),
     "cn_read_output": ([_vp, _vp], _i),
@@ -115,6 +119,27 @@ def check(rc, what=""):
         msg = lib().cn_last_error().decode(errors="replace")
         raise ChestnutError(f"{what or 'chestnut call'} failed ({rc}): {msg}")
     return rc
+
+
+class PinnedArray:
+    """A numpy array over page-locked host memory (cn_host_alloc_pinned), so
+    the engine's copies to and from it are asynchronous.  .array is the view;
+    free() releases the memory (the view must not be used after it)."""
+
+    def __init__(self, shape, dtype):
+        import numpy as np
+        dt = np.dtype(dtype)
+        n = int(np.prod(shape)) * dt.itemsize
+        p = ctypes.c_void_p()
+        check(lib().cn_host_alloc_pinned(ctypes.byref(p), max(n, 1)), "cn_host_alloc_pinned")
+        self.ptr = p
+        self.array = np.frombuffer((ctypes.c_uint8 * max(n, 1)).from_address(p.value), dt, count=int(np.prod(shape))
+                                   ).reshape(shape)
+
+    def free(self):
+        if self.ptr is not None and self.ptr.value:
+            lib().cn_host_free_pinned(self.ptr)
+        self.ptr = None
 
 
 class DeviceBuffer:

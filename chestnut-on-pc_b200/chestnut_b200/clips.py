@@ -16,6 +16,8 @@ import os
 
 import numpy as np
 
+FRAME_OUT = 3323  # floats of one frame's flat output (plan | lane_lines | lead | hidden_state)
+
 
 def assign(n_clips, world, rank):
     """Clip ids owned by `rank` (round robin)."""
@@ -35,7 +37,9 @@ def run_rank(engine_factory, frame_source, clips, n_frames, batch, batch_source=
     (the hidden state is carried here exactly as video_check.py:60 does);
     batch_source(group, frame), when given, returns the whole batch at once
     (warped u8[B,2,6,128,256], packed f32[B,524]) so callers can pre-assemble
-    inputs.
+    inputs; with an engine that stages inputs (stage / run_staged), the next
+    frame's warped batch is then uploaded while the current frame runs (the
+    warped bytes do not depend on the carried hidden state).
     """
     results = {}
     engines = {}
@@ -49,7 +53,19 @@ def run_rank(engine_factory, frame_source, clips, n_frames, batch, batch_source=
         hidden = np.zeros((B, 512), np.float32)
         sums = np.zeros((B, n_frames), np.float64)
         out = None
+        staged = batch_source is not None and hasattr(eng, "stage")
+        if staged and n_frames > 0:
+            eng.stage(batch_source(group, 0)[0])
         for f in range(n_frames):
+            if staged:
+                if f + 1 < n_frames:
+                    eng.stage(batch_source(group, f + 1)[0])
+                pk = batch_source(group, f)[1]
+                pk[:, 12:] = hidden
+                out = np.asarray(eng.run_staged(pk)).reshape(B, -1)
+                hidden = out[:, -512:].copy()
+                sums[:, f] = out.astype(np.float64).sum(axis=1)
+                continue
             if batch_source is not None:
                 w, pk = batch_source(group, f)
             else:
@@ -63,6 +79,48 @@ def run_rank(engine_factory, frame_source, clips, n_frames, batch, batch_source=
             sums[:, f] = out.astype(np.float64).sum(axis=1)
         for i, c in enumerate(group):
             results[c] = (sums[i], out[i].copy())
+    return results
+
+
+def run_rank_pipelined(engine_factory, clips, n_frames, batch, batch_source, alloc):
+    """run_rank for engines that carry the hidden state on the device and
+    queue frames (stage / run_staged_async / wait_output): frame f+1 is
+    uploaded and queued before the host reads frame f's output, so the host's
+    per-frame work overlaps the GPU.  Same results as run_rank (the device
+    carry equals the host carry bit for bit).  alloc(shape, dtype) returns an
+    array in pinned host memory (outputs and packed vectors are copied
+    asynchronously)."""
+    results = {}
+    engines = {}
+    bufs = {}
+    for group in batches(clips, batch):
+        B = len(group)
+        eng = engines.get(B)
+        if eng is None:
+            eng = engines[B] = engine_factory(B)
+        elif hasattr(eng, "reset"):
+            eng.reset()  # a new clip group starts from empty queues and a zero hidden state
+        if B not in bufs:
+            bufs[B] = ([alloc((B, FRAME_OUT), np.float32) for _ in range(2)],
+                       [alloc((B, 524), np.float32) for _ in range(2)])
+        outs, pks = bufs[B]
+        sums = np.zeros((B, n_frames), np.float64)
+        if n_frames == 0:
+            continue
+        eng.stage(batch_source(group, 0)[0])
+        for f in range(n_frames):
+            if f + 1 < n_frames:
+                eng.stage(batch_source(group, f + 1)[0])
+            pks[f % 2][:] = batch_source(group, f)[1]
+            eng.run_staged_async(pks[f % 2], outs[f % 2])
+            if f > 0:
+                eng.wait_output()
+                sums[:, f - 1] = outs[(f - 1) % 2].sum(axis=1, dtype=np.float64)
+        eng.wait_output()
+        last = outs[(n_frames - 1) % 2]
+        sums[:, n_frames - 1] = last.sum(axis=1, dtype=np.float64)
+        for i, c in enumerate(group):
+            results[c] = (sums[i], last[i].copy())
     return results
 
 

@@ -58,6 +58,7 @@ class Engine:
         h = ctypes.c_void_p()
         check(lib().cn_engine_create(ctypes.byref(cfg), ctypes.byref(h)), "cn_engine_create")
         self._h = h
+        self.carry_hidden = bool(carry_hidden)
         self.out_slices = output_slices()
         self.n_out = _lib.N_OUT
 
@@ -71,6 +72,35 @@ class Engine:
             out = np.empty((self.batch, self.n_out) if self.batch > 1 else (self.n_out,), np.float32)
         check(lib().cn_run_frame(self._h, w.ctypes.data, p.ctypes.data, out.ctypes.data), "cn_run_frame")
         return out
+
+    def stage(self, warped):
+        """Start uploading the next frame's warped bytes (double-buffered; the
+        array must stay alive and unchanged until run_staged consumes it, and
+        be in pinned memory for the copy to overlap compute)."""
+        w = warped if isinstance(warped, int) else np.ascontiguousarray(warped, np.uint8)
+        if not isinstance(w, int):
+            assert w.size == self.batch * _lib.FRAME_BYTES, w.shape
+        check(lib().cn_stage_input(self._h, w if isinstance(w, int) else w.ctypes.data), "cn_stage_input")
+
+    def run_staged(self, packed, out=None):
+        """run_frame on the oldest staged input."""
+        p = np.ascontiguousarray(packed, np.float32)
+        assert p.size == self.batch * _lib.PACKED, p.shape
+        if out is None:
+            out = np.empty((self.batch, self.n_out) if self.batch > 1 else (self.n_out,), np.float32)
+        check(lib().cn_run_staged(self._h, p.ctypes.data, out.ctypes.data), "cn_run_staged")
+        return out
+
+    def run_staged_async(self, packed, out):
+        """Queue a frame on the oldest staged input; its output lands in
+        `out` (a pinned array, see PinnedArray) once wait_output returns."""
+        p = np.ascontiguousarray(packed, np.float32)
+        assert p.size == self.batch * _lib.PACKED, p.shape
+        assert out.size == self.batch * self.n_out and out.dtype == np.float32
+        check(lib().cn_run_staged_async(self._h, p.ctypes.data, out.ctypes.data), "cn_run_staged_async")
+
+    def wait_output(self):
+        check(lib().cn_wait_output(self._h), "cn_wait_output")
 
     def run_frame_async(self, warped_ptr, packed_ptr):
         """Host pointers (ideally pinned); output stays on the device."""

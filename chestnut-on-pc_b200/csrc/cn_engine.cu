@@ -179,6 +179,16 @@ struct cn_engine {
   int pending = 0;               // a frame is in flight
   float* dec = nullptr;          // decoded outputs (cn_decode_frame), allocated on first use
   size_t dec_floats = 0;
+  // double-buffered input (cn_stage_input / cn_run_staged), allocated on first use
+  uint8_t* stage_buf = nullptr;  // [2][B][warped]
+  cudaStream_t copy = nullptr;
+  cudaEvent_t stage_ready[2] = {nullptr, nullptr}, stage_free[2] = {nullptr, nullptr};
+  int stage_head = 0, stage_count = 0;
+  // frames queued by cn_run_staged_async: output-copied events and the
+  // device error word of each (pinned)
+  cudaEvent_t out_ev[2] = {nullptr, nullptr};
+  int* err_host = nullptr;
+  int out_head = 0, out_count = 0;
 };
 
 namespace cn {
@@ -872,6 +882,18 @@ int cn_engine_destroy(cn_engine* e) {
   if (e->wblob) cudaFree(e->wblob);
   if (e->ablob) cudaFree(e->ablob);
   if (e->dec) cudaFree(e->dec);
+  if (e->copy) {
+    cudaStreamSynchronize(e->copy);
+    cudaStreamDestroy(e->copy);
+  }
+  for (int i = 0; i < 2; ++i) {
+    if (e->stage_ready[i]) cudaEventDestroy(e->stage_ready[i]);
+    if (e->stage_free[i]) cudaEventDestroy(e->stage_free[i]);
+  }
+  if (e->stage_buf) cudaFree(e->stage_buf);
+  for (int i = 0; i < 2; ++i)
+    if (e->out_ev[i]) cudaEventDestroy(e->out_ev[i]);
+  if (e->err_host) cudaFreeHost(e->err_host);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
   return 0;
@@ -1001,6 +1023,111 @@ int cn_run_frame(cn_engine* e, const uint8_t* warped, const float* packed, float
   CN_CUDA(cudaSetDevice(e->cfg.device));
   CN_CUDA(cudaMemcpyAsync(e->d_warped, warped, (size_t)e->B * kWarpedBytes, cudaMemcpyHostToDevice, e->stream));
   CN_CUDA(cudaMemcpyAsync(e->d_packed, packed, (size_t)e->B * kPacked * 4, cudaMemcpyHostToDevice, e->stream));
+  CN_TRY(launch_frame(e));
+  if (!out) {
+    e->pending = 1;
+    return 0;
+  }
+  return cn_read_output(e, out);
+}
+
+int cn_stage_input(cn_engine* e, const uint8_t* warped) {
+  if (!e || !warped) {
+    set_last_error("cn_stage_input: null argument");
+    return CN_ERR_ARG;
+  }
+  if (e->stage_count >= 2) {
+    set_last_error("cn_stage_input: two inputs are already staged (run one with cn_run_staged first)");
+    return CN_ERR_ARG;
+  }
+  CN_CUDA(cudaSetDevice(e->cfg.device));
+  const size_t bytes = (size_t)e->B * kWarpedBytes;
+  if (!e->stage_buf) {
+    CN_CUDA(cudaMalloc((void**)&e->stage_buf, 2 * bytes));
+    CN_CUDA(cudaStreamCreateWithFlags(&e->copy, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; ++i) {
+      CN_CUDA(cudaEventCreateWithFlags(&e->stage_ready[i], cudaEventDisableTiming));
+      CN_CUDA(cudaEventCreateWithFlags(&e->stage_free[i], cudaEventDisableTiming));
+      CN_CUDA(cudaEventRecord(e->stage_free[i], e->stream));
+    }
+  }
+  const int slot = (e->stage_head + e->stage_count) & 1;
+  // the slot's previous contents have been moved out by the frame that used them
+  CN_CUDA(cudaStreamWaitEvent(e->copy, e->stage_free[slot], 0));
+  CN_CUDA(cudaMemcpyAsync(e->stage_buf + slot * bytes, warped, bytes, cudaMemcpyHostToDevice, e->copy));
+  CN_CUDA(cudaEventRecord(e->stage_ready[slot], e->copy));
+  ++e->stage_count;
+  return 0;
+}
+
+// The staged input of the oldest cn_stage_input -> the engine's input buffer
+// on its stream, then the packed vector; the caller launches the frame.
+static int take_staged(cn_engine* e, const float* packed) {
+  const size_t bytes = (size_t)e->B * kWarpedBytes;
+  const int slot = e->stage_head;
+  CN_CUDA(cudaStreamWaitEvent(e->stream, e->stage_ready[slot], 0));
+  CN_CUDA(cudaMemcpyAsync(e->d_warped, e->stage_buf + slot * bytes, bytes, cudaMemcpyDeviceToDevice, e->stream));
+  CN_CUDA(cudaEventRecord(e->stage_free[slot], e->stream));
+  e->stage_head ^= 1;
+  --e->stage_count;
+  CN_CUDA(cudaMemcpyAsync(e->d_packed, packed, (size_t)e->B * kPacked * 4, cudaMemcpyHostToDevice, e->stream));
+  return 0;
+}
+
+int cn_run_staged_async(cn_engine* e, const float* packed, float* out) {
+  if (!e || !packed || !out) {
+    set_last_error("cn_run_staged_async: null argument");
+    return CN_ERR_ARG;
+  }
+  if (e->stage_count == 0 || e->out_count >= 2) {
+    set_last_error("cn_run_staged_async: %s", e->stage_count == 0 ? "no input staged (cn_stage_input first)"
+                                                                  : "two frames already queued (cn_wait_output first)");
+    return CN_ERR_ARG;
+  }
+  CN_CUDA(cudaSetDevice(e->cfg.device));
+  if (!e->err_host) {
+    CN_CUDA(cudaHostAlloc((void**)&e->err_host, 2 * sizeof(int), cudaHostAllocDefault));
+    for (int i = 0; i < 2; ++i) CN_CUDA(cudaEventCreateWithFlags(&e->out_ev[i], cudaEventDisableTiming));
+  }
+  CN_TRY(take_staged(e, packed));
+  CN_TRY(launch_frame(e));
+  const int slot = (e->out_head + e->out_count) & 1;
+  CN_CUDA(cudaMemcpyAsync(out, e->out, (size_t)e->B * kNOut * 4, cudaMemcpyDeviceToHost, e->stream));
+  CN_CUDA(cudaMemcpyFromSymbolAsync(&e->err_host[slot], g_cn_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost,
+                                    e->stream));
+  CN_CUDA(cudaEventRecord(e->out_ev[slot], e->stream));
+  ++e->out_count;
+  return 0;
+}
+
+int cn_wait_output(cn_engine* e) {
+  if (!e || e->out_count == 0) {
+    set_last_error("cn_wait_output: no frame queued");
+    return CN_ERR_ARG;
+  }
+  CN_CUDA(cudaSetDevice(e->cfg.device));
+  const int slot = e->out_head;
+  CN_CUDA(cudaEventSynchronize(e->out_ev[slot]));
+  e->out_head ^= 1;
+  --e->out_count;
+  if (e->err_host[slot]) {
+    set_last_error("device-side error code %d (a bounded wait expired inside a kernel)", e->err_host[slot]);
+    return CN_ERR_DEVICE;
+  }
+  return 0;
+}
+
+int cn_run_staged(cn_engine* e, const float* packed, float* out) {
+  if (!e || !packed) {
+    set_last_error("cn_run_staged: null argument");
+    return CN_ERR_ARG;
+  }
+  if (e->stage_count == 0) {
+    set_last_error("cn_run_staged: no input staged (cn_stage_input first)");
+    return CN_ERR_ARG;
+  }
+  CN_CUDA(cudaSetDevice(e->cfg.device));
+  CN_TRY(take_staged(e, packed));
   CN_TRY(launch_frame(e));
   if (!out) {
     e->pending = 1;

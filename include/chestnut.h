@@ -90,6 +90,26 @@ int cn_engine_destroy(cn_engine* e);
  * out: host f32 [batch][CN_N_OUT] or NULL (the frame is then left in flight
  * and its output on the device; read it with cn_read_output). */
 int cn_run_frame(cn_engine* e, const uint8_t* warped, const float* packed, float* out);
+/* Double-buffered input (no counterpart in the reference, whose run_frame is
+ * the only entry): cn_stage_input starts copying the next frame's warped
+ * bytes (host u8 [batch][2][6][128][256]; pinned memory, or the copy is not
+ * asynchronous) to the engine on a copy stream and returns at once;
+ * cn_run_staged runs a frame, exactly as cn_run_frame would, on the oldest
+ * staged input.  So the upload of frame f+1 overlaps the compute of frame f.
+ * At most two inputs are staged ahead (CN_ERR_ARG beyond that, and for
+ * cn_run_staged with nothing staged); the host buffer must stay unchanged
+ * until the cn_run_staged call that consumes it returns. */
+int cn_stage_input(cn_engine* e, const uint8_t* warped);
+int cn_run_staged(cn_engine* e, const float* packed, float* out);
+/* cn_run_staged without waiting: the frame and the copy of its output into
+ * `out` (pinned host memory, B x CN_N_OUT f32) are queued and the call
+ * returns; cn_wait_output waits for the oldest queued frame (at most two
+ * queued) and reports a device-side error of that frame.  With the hidden
+ * state carried on the device (cn_config.carry_hidden) nothing the host does
+ * between frames depends on the previous output, so frame f+1 runs while the
+ * host consumes frame f. */
+int cn_run_staged_async(cn_engine* e, const float* packed, float* out);
+int cn_wait_output(cn_engine* e);
 /* n frames back to back with the hidden state carried by the caller's rule
  * packed[12:] = out[hidden_state] (video_check.py:60); outs: [n][batch][N_OUT]. */
 int cn_run_frames(cn_engine* e, int n, const uint8_t* warped, const float* packed0, float* outs);

@@ -128,3 +128,53 @@ def test_comm_library_exports_and_argument_errors():
     import re
     for name in re.findall(r"^int (cn_comm_\w+)\(", hdr, re.M):
         assert hasattr(L, name), name
+
+
+class FakeQueuedEngine(FakeEngine):
+    """FakeEngine with the queued interface: staged inputs, the hidden state
+    carried on the 'device' (the previous output), outputs written into the
+    caller's buffers only when waited for, as the asynchronous copies would."""
+
+    def __init__(self, batch):
+        super().__init__(batch)
+        self.staged, self.queued = [], []
+        self.prev = np.zeros((batch, N_OUT), np.float32)
+
+    def reset(self):
+        self.prev = np.zeros((self.batch, N_OUT), np.float32)
+
+    def stage(self, warped):
+        assert len(self.staged) < 2
+        self.staged.append(np.array(warped, copy=True))
+
+    def run_staged_async(self, packed, out):
+        assert len(self.queued) < 2
+        pk = np.array(packed, copy=True)
+        pk[:, 12:] = self.prev[:, -512:]
+        res = self.run_frame(self.staged.pop(0), pk)
+        self.prev = res
+        self.queued.append((out, res))
+
+    def wait_output(self):
+        out, res = self.queued.pop(0)
+        out[:] = res
+
+
+def test_pipelined_runner_equals_host_carry_runner():
+    group = [3, 5, 8, 11, 12]
+    cache = {}
+
+    def batch_source(g, f):
+        key = (tuple(g), f)
+        if key not in cache:
+            ws, pks = zip(*(frame_source(c, f) for c in g))
+            cache[key] = (np.stack(ws), np.stack(pks))
+        w, pk = cache[key]
+        return w, pk.copy()
+
+    ref = clips.run_rank(FakeEngine, None, group, 6, 2, batch_source)
+    got = clips.run_rank_pipelined(FakeQueuedEngine, group, 6, 2, batch_source, lambda s, d: np.zeros(s, d))
+    assert sorted(ref) == sorted(got) == sorted(group)
+    for c in group:
+        assert np.array_equal(ref[c][0], got[c][0]), c
+        assert np.array_equal(ref[c][1], got[c][1]), c

@@ -186,3 +186,66 @@ def test_1b_frames_match_oracle():
         assert all(ok for _, ok in errs.values()), (f, errs)
         pg[12:] = got[spec.out_slices()["hidden_state"]]
         po[12:] = ref[spec.out_slices()["hidden_state"]]
+
+
+def test_staged_input_equals_run_frame():
+    # cn_stage_input / cn_run_staged: the next frame's upload overlaps the
+    # current frame; the outputs are those of cn_run_frame, bit for bit
+    from chestnut_b200._lib import ChestnutError
+    rs = np.random.default_rng(14)
+    B = 2
+    w = rs.integers(0, 256, (5, B, 2, 6, 128, 256), dtype=np.uint8)
+    pk = np.zeros((5, B, 524), np.float32)
+    pk[:, :, 3] = 1.0
+    pk[:, :, 8] = 1.0
+    a, b = Engine("39m", seed=4, batch=B), Engine("39m", seed=4, batch=B)
+    with pytest.raises(ChestnutError):
+        b.run_staged(pk[0])                      # nothing staged yet
+    b.stage(w[0])
+    for f in range(5):
+        if f + 1 < 5:
+            b.stage(w[f + 1])
+        if f == 0:
+            with pytest.raises(ChestnutError):
+                b.stage(w[0])                    # at most two inputs ahead
+        oa = a.run_frame(w[f], pk[f])
+        ob = b.run_staged(pk[f])
+        assert np.array_equal(oa, ob), f
+
+
+def test_pipelined_clip_runner_equals_run_frame_runner():
+    # device-carried hidden state + queued frames (cn_run_staged_async /
+    # cn_wait_output) give the host-carry run_frame results bit for bit
+    from chestnut_b200 import PinnedArray, clips
+    rs = np.random.default_rng(21)
+    pool = rs.integers(0, 256, (3, 2, 6, 128, 256), dtype=np.uint8)
+    pins = []
+
+    def alloc(shape, dtype):
+        pins.append(PinnedArray(shape, dtype))
+        return pins[-1].array
+
+    staged = {}
+
+    def batch_source(group, f):
+        key = (tuple(group), f % 3)
+        if key not in staged:
+            w = alloc((len(group), 2, 6, 128, 256), np.uint8)
+            w[:] = np.stack([pool[(c + f) % 3] for c in group])
+            pk = np.zeros((len(group), 524), np.float32)
+            for i, c in enumerate(group):
+                pk[i, c % 8] = 1.0
+                pk[i, 8] = 1.0
+            staged[key] = (w, pk)
+        w, pk = staged[key]
+        return w, pk.copy()
+
+    group = [0, 1, 2]
+    ref = clips.run_rank(lambda n: Engine("39m", seed=6, batch=n), None, group, 7, 3, batch_source)
+    got = clips.run_rank_pipelined(lambda n: Engine("39m", seed=6, batch=n, carry_hidden=True), group, 7, 3,
+                                   batch_source, alloc)
+    for c in group:
+        assert np.array_equal(ref[c][0], got[c][0]), c
+        assert np.array_equal(ref[c][1], got[c][1]), c
+    for p in pins:
+        p.free()
