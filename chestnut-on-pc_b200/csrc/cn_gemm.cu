@@ -476,9 +476,14 @@ int launch_plan(const GemmPlan& g, cudaStream_t stream) {
 // split-K staging / receive tiles and the prefetched residual rows.
 static void gemm_smem_layout(int bn, int K, int splits, bool prefetch, int* stages, int* region, size_t* smem) {
   const int stage = kA_Bytes + bn * 128;
-  const int maxst = bn == 256 ? 4 : (bn == 128 ? 6 : 8);
   const int kb = (K + 63) / 64;
   const int per = (kb + splits - 1) / splits;
+  // Unsplit CTAs with a short K keep a short ring (~96 KB) so that two or
+  // three share an SM: one CTA's epilogue then overlaps another's main loop.
+  // Long-K CTAs and split-K clusters (weight-streaming GEMMs of a few rows)
+  // keep deep rings.
+  const bool shallow = splits == 1 && per <= 12;
+  const int maxst = shallow ? (bn == 256 ? 2 : 3) : (bn == 256 ? 4 : (bn == 128 ? 6 : 8));
   const int st = per < 2 ? 2 : (per > maxst ? maxst : per);
   const int ch = bn < 128 ? bn : 128;
   const int rpo = (128 + splits - 1) / splits;
