@@ -433,11 +433,25 @@ static int layout_acts(cn_engine* e) {
   want((void**)&e->rings.desire, (size_t)B * kDesireQ * kDesire * 4);
   want((void**)&e->rings.ctr, 256);
   want((void**)&e->a0, (size_t)2 * B * 8192 * kK0Pad * 2);
+  if (e->use_stem) {
+    // plan over the (not yet placed) activations: does the persistent stem
+    // cover these shapes, and how large are its split-K partials?
+    StemPlan* dry = new StemPlan;
+    if (stem_build(e, dry) == 0) {
+      e->spart_floats = dry->part_floats;
+      want((void**)&e->spart, (size_t)e->spart_floats * 4 + 16);
+      want((void**)&e->sctr, stem_counter_bytes());
+    } else {
+      e->use_stem = false;  // shapes the persistent stem does not cover: per-layer stem kernels
+    }
+    delete dry;
+  }
   int cin = 12;
   for (int s = 0; s < 5; ++s) {
     const size_t P = (size_t)(64 >> s) * (128 >> s);
-    if (s > 0) want((void**)&e->gat[s], 2 * B * P * 9 * cin * 2);
-    else e->gat[0] = nullptr;
+    // im2col matrices: per-layer stem only (the persistent stem gathers in its loads)
+    e->gat[s] = nullptr;
+    if (s > 0 && !e->use_stem) want((void**)&e->gat[s], 2 * B * P * 9 * cin * 2);
     want((void**)&e->y3[s], 2 * B * P * m.stem[s] * 2);
     want((void**)&e->act[s], 2 * B * P * m.stem[s] * 2);
     cin = m.stem[s];
@@ -460,18 +474,6 @@ static int layout_acts(cn_engine* e) {
     want((void**)&e->h2, R * m.d * 2);
     e->tctr_bytes = trunk_counter_bytes(m.layers);
     want((void**)&e->tctr, e->tctr_bytes);
-  }
-  if (e->use_stem) {
-    // size the partials with a plan over the (not yet placed) activations
-    StemPlan* dry = new StemPlan;
-    if (stem_build(e, dry) == 0) {
-      e->spart_floats = dry->part_floats;
-      want((void**)&e->spart, (size_t)e->spart_floats * 4 + 16);
-      want((void**)&e->sctr, stem_counter_bytes());
-    } else {
-      e->use_stem = false;  // shapes the persistent stem does not cover: per-layer stem kernels
-    }
-    delete dry;
   }
   for (auto& r : req) off += align256(r.second);
   e->abytes = off;
@@ -942,9 +944,11 @@ int cn_engine_create(const cn_config* cfg, cn_engine** out) {
     {
       const char* tv = getenv("CN_TRUNK");
       e->use_trunk = trunk_supported(e->B * kT, e->m.d, e->m.heads) && !(tv && tv[0] == '0');
-      // the conv stem as one persistent kernel as well; CN_STEM=0 selects the per-layer kernels
+      // the conv stem as one persistent kernel (any number of clips; batched
+      // clips then run the per-layer transformer kernels); CN_STEM=0 selects
+      // the per-layer stem kernels
       const char* sv = getenv("CN_STEM");
-      e->use_stem = e->use_trunk && e->B == 1 && !(sv && sv[0] == '0');
+      e->use_stem = !(sv && sv[0] == '0');
     }
     layout_weights(e);
     if (cudaMalloc((void**)&e->wblob, e->wbytes) != cudaSuccess) {

@@ -682,9 +682,9 @@ __global__ void __launch_bounds__(kStThreads, 1)
                 CN_ST(p, 11);
               }
             } else {
-              // f32 / token tiles (at most 32 rows): the warps holding valid
-              // rows stage the accumulators in Y ([row][BN + 4] f32), then all
-              // four warps emit 8-feature groups
+              // f32 / token tiles (at most 64 features wide): the warps
+              // holding valid rows stage the accumulators in Y ([row][BN + 4]
+              // f32), then all four warps emit 8-feature groups
               float* sacc = reinterpret_cast<float*>(Y);
               const int ld = BN + 4;
               if (live && 32 * q < rv)
@@ -893,10 +893,12 @@ int stem_add(StemPlan* sp, const StemSpec& s) {
   // so that more CTAs share the epilogue.
   const int KB = (s.K + 63) / 64;
   const bool split = !fuse && KB > kStMaxUnsplitKb;
+  // f32 / token epilogues stage a whole tile in Y ([rows][BN + 4] f32): a
+  // full 128-row tile is 64 features wide.
   if (fuse)
     P.BN = s.N;
   else if (!split)
-    P.BN = std::min(s.N, s.Mg >= 128 ? 128 : 64);
+    P.BN = std::min(s.N, s.Mg >= 128 && s.epi == SE_RELU_F16 ? 128 : 64);
   else
     P.BN = s.Mg >= 128 ? std::min(s.N, 128) : std::min(s.N, 256);
   P.tm = (s.Mg + 127) / 128;

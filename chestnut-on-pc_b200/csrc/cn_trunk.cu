@@ -155,12 +155,21 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) 
                : "memory");
 }
 
-// Spin until *ctr >= target (bounded).  false on timeout or a recorded error.
+// Counters are monotonic across launches and their targets grow with a launch
+// epoch, so both wrap around; a counter never trails its target by 2^31 or
+// more (it trails by at most the units of one launch), so the signed
+// difference orders them.
+__device__ __forceinline__ bool ctr_reached(unsigned v, unsigned target) { return (int)(v - target) >= 0; }
+__device__ __forceinline__ bool ctr_reached(unsigned long long v, unsigned long long target) {
+  return (long long)(v - target) >= 0;
+}
+
+// Spin until *ctr has reached target (bounded).  false on timeout or a recorded error.
 template <typename T, typename Ld>
 __device__ __forceinline__ bool spin_until(const T* ctr, T target, int code, Ld ld) {
-  if (ld(ctr) >= target) return true;
+  if (ctr_reached(ld(ctr), target)) return true;
   const unsigned long long t0 = global_ns();
-  while (ld(ctr) < target) {
+  while (!ctr_reached(ld(ctr), target)) {
     if (dev_error_set()) return false;
     if (global_ns() - t0 > kWaitLimitNs) {
       set_dev_error(code);

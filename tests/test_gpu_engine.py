@@ -39,18 +39,21 @@ def params39():
     return omodel.gen_params(spec.CONFIGS["39m"], 3)
 
 
-@pytest.mark.parametrize("mode", ["persistent", "per-layer stem", "per-layer"])
+@pytest.mark.parametrize("mode", ["persistent", "per-layer stem", "per-layer trunk", "per-layer"])
 def test_39m_frames_match_oracle_with_hidden_carry(params39, mode, monkeypatch):
     # single-clip engines run the conv stem and the transformer as one
-    # persistent kernel each unless CN_STEM=0 / CN_TRUNK=0
-    monkeypatch.setenv("CN_TRUNK", "0" if mode == "per-layer" else "1")
-    monkeypatch.setenv("CN_STEM", "1" if mode == "persistent" else "0")
+    # persistent kernel each unless CN_STEM=0 / CN_TRUNK=0 ("per-layer trunk"
+    # is the combination batched clips run)
+    trunk = mode in ("persistent", "per-layer stem")
+    stem = mode in ("persistent", "per-layer trunk")
+    monkeypatch.setenv("CN_TRUNK", "1" if trunk else "0")
+    monkeypatch.setenv("CN_STEM", "1" if stem else "0")
     rs = np.random.default_rng(0)
     w, pk = frame_inputs(rs, 12)
     eng = Engine("39m", seed=3)
     names = [k["name"] for k in eng.kernel_list()]
-    assert ("transformer_trunk" in names) == (mode != "per-layer")
-    assert ("conv_stem" in names) == (mode == "persistent")
+    assert ("transformer_trunk" in names) == trunk
+    assert ("conv_stem" in names) == stem
     clip = omodel.Clip("39m", 3, params39)
     pg, po = pk[0].copy(), pk[0].copy()
     for f in range(len(w)):
@@ -130,6 +133,32 @@ def test_batched_clips_match_single_clip_engines():
             assert all(ok for _, ok in errs.values()), (f, b, errs)
 
 
+@pytest.mark.parametrize("B", [5, 16])
+def test_batched_persistent_stem_matches_per_layer_stem(B, monkeypatch):
+    # 5 clips: ragged tiles (stage 4's 160 rows, 120 temporal-token rows, 5
+    # cond rows) and 128-row tiles spanning several images; 16: whole tiles
+    rs = np.random.default_rng(11)
+    n = 3
+    w = rs.integers(0, 256, (n, B, 2, 6, 128, 256), dtype=np.uint8)
+    pk = np.zeros((n, B, 524), np.float32)
+    pk[:, :, 8] = 1
+    pk[:, :, 10:12] = rs.standard_normal((n, B, 2))
+    for f in range(n):
+        for b in range(B):
+            pk[f, b, (f + b) % 8] = 1
+    a, c = Engine("39m", seed=7, batch=B), Engine("39m", seed=7, batch=B, use_graph=False)
+    assert "conv_stem" in [k["name"] for k in a.kernel_list()]
+    monkeypatch.setenv("CN_STEM", "0")
+    ref = Engine("39m", seed=7, batch=B)
+    assert "conv_stem" not in [k["name"] for k in ref.kernel_list()]
+    for f in range(n):
+        oa, oc, orf = a.run_frame(w[f], pk[f]), c.run_frame(w[f], pk[f]), ref.run_frame(w[f], pk[f])
+        assert np.array_equal(oa, oc), f          # graph replay == eager, run to run identical
+        for b in range(B):
+            errs = head_errors(oa[b], orf[b])
+            assert all(ok for _, ok in errs.values()), (f, b, errs)
+
+
 def test_kernel_list_describes_the_frame(monkeypatch):
     # the conv stem with the cond and token embeddings as one persistent
     # launch; the transformer, the final LayerNorm, the token mean and the
@@ -146,13 +175,22 @@ def test_kernel_list_describes_the_frame(monkeypatch):
     assert sum(n.startswith("border_gather_s2") for n in names) == 4
     assert names.count("transformer_trunk") == 1
     assert "token_mean_pool" not in names and "layernorm:final" not in names
-    monkeypatch.delenv("CN_STEM")
     # per-layer kernels: 4 GEMMs per layer, then final LN, pool and 3 head GEMMs
     monkeypatch.setenv("CN_TRUNK", "0")
     names = [k["name"] for k in Engine("39m", seed=0).kernel_list()]
     assert sum(n.startswith("gemm_tc") for n in names) == 10 + 3 + 4 * 4 + 3
     assert "transformer_trunk" not in names
     assert "token_mean_pool" in names and "layernorm:final" in names
+    # the persistent stem before the per-layer transformer kernels
+    monkeypatch.delenv("CN_STEM")
+    names = [k["name"] for k in Engine("39m", seed=0).kernel_list()]
+    assert names[:3] == ["queue_push", "border_gather0", "conv_stem"]
+    assert sum(n.startswith("gemm_tc") for n in names) == 4 * 4 + 3
+    monkeypatch.delenv("CN_TRUNK")
+    # batched clips: the persistent stem, then the per-layer transformer kernels
+    names = [k["name"] for k in Engine("39m", seed=0, batch=3).kernel_list()]
+    assert names[:3] == ["queue_push", "border_gather0", "conv_stem"]
+    assert "transformer_trunk" not in names and not any(n.startswith("border_gather_s2") for n in names)
 
 
 @pytest.mark.parametrize("cfg", ["39m", "1b"])
@@ -161,6 +199,7 @@ def test_persistent_kernels_are_deterministic_and_match_per_layer_kernels(cfg, m
     w, pk = frame_inputs(rs, 4)
     a, b = Engine(cfg, seed=5), Engine(cfg, seed=5, use_graph=False)
     monkeypatch.setenv("CN_TRUNK", "0")
+    monkeypatch.setenv("CN_STEM", "0")
     ref = Engine(cfg, seed=5)
     for f in range(4):
         oa, ob, orf = a.run_frame(w[f], pk[f]), b.run_frame(w[f], pk[f]), ref.run_frame(w[f], pk[f])
