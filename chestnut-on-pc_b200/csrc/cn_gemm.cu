@@ -136,6 +136,46 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const float*
   }
 }
 
+// f16 epilogue of an unsplit tile straight from the TMEM registers: thread =
+// accumulator row (lane quadrant = warp), 16 columns per tcgen05.ld; bias and
+// activation, then the row's 16-column segment as two 16-byte stores.  No
+// staging through shared memory, no per-element bounds checks (the host
+// enables it only for N % 16 == 0 and 16-byte aligned rows).  The arithmetic
+// is the staged epilogue's: f16(act(acc + bias)).
+template <int BN, int ACT>
+__device__ __forceinline__ void epilogue_direct(const GemmParams& p, uint32_t tmem, int m_tile, int n_tile,
+                                                int group) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long m = (long long)m_tile * 128 + warp * 32 + lane;
+  const bool live = m < p.M;
+  const float* bias = p.bias ? p.bias + (long long)group * p.bias_gstride : nullptr;
+  __half* out = reinterpret_cast<__half*>(p.out) + (long long)group * p.out_gstride + m * p.ldo;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 16) {
+    const int n = n_tile * BN + c;
+    if (n >= p.N) break;  // warp-uniform: tcgen05.ld is .aligned
+    uint32_t r[16];
+    tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, r);
+    tmem_ld_wait();
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+    if (bias) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(bias + n) + q);
+        v[4 * q] += b.x; v[4 * q + 1] += b.y; v[4 * q + 2] += b.z; v[4 * q + 3] += b.w;
+      }
+    }
+    if (!live) continue;
+    __align__(16) __half h[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) h[j] = __float2half_rn(apply_act(v[j], ACT));
+    reinterpret_cast<uint4*>(out + n)[0] = reinterpret_cast<const uint4*>(h)[0];
+    reinterpret_cast<uint4*>(out + n)[1] = reinterpret_cast<const uint4*>(h)[1];
+  }
+}
+
 // BM: layout of B -- 0 K-major [N][K], 1 MN-major [K][N], 2 k-blocked [KB][N][64].
 template <int BN, int BM, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -265,6 +305,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (S > 1) cluster_sync(); else __syncthreads();
   tc_fence_after();
 
+  bool direct = false;
+  if constexpr (EPI == EPI_F16) {
+    direct = p.direct != 0;
+    if (direct) {
+      pdl_wait();  // the epilogue reads / writes activations of earlier kernels
+      switch (p.act) {
+        case ACT_RELU: epilogue_direct<BN, ACT_RELU>(p, tmem, m_tile, n_tile, group); break;
+        case ACT_GELU: epilogue_direct<BN, ACT_GELU>(p, tmem, m_tile, n_tile, group); break;
+        case ACT_TANH: epilogue_direct<BN, ACT_TANH>(p, tmem, m_tile, n_tile, group); break;
+        default: epilogue_direct<BN, ACT_NONE>(p, tmem, m_tile, n_tile, group); break;
+      }
+    }
+  }
+  if (!direct) {
   // ---- post-MMA, per column chunk.  Shared memory (pipeline buffers are free
   // now): staging [S][rpo][LdC] f32 = this CTA's partial rows grouped by owner
   // rank; recv [S][rpo][LdC] = the peers' partials of the owned rows;
@@ -339,6 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Peers' bulk copies out of this CTA's staging tile have landed once every
   // CTA of the cluster has received its last chunk.
   if (S > 1) cluster_wait();
+  }
 
   // Error path: do not leave a TMA write in flight into freed shared memory.
   if (warp == 0 && lane == 0 && g_cn_dev_error != 0) {
@@ -474,7 +529,8 @@ int launch_plan(const GemmPlan& g, cudaStream_t stream) {
 // Pipeline depth follows the k-blocks a CTA actually streams (short-K GEMMs
 // then fit several CTAs per SM); after the main loop the same region holds the
 // split-K staging / receive tiles and the prefetched residual rows.
-static void gemm_smem_layout(int bn, int K, int splits, bool prefetch, int* stages, int* region, size_t* smem) {
+static void gemm_smem_layout(int bn, int K, int splits, bool prefetch, int* stages, int* region, size_t* smem,
+                             bool direct = false) {
   const int stage = kA_Bytes + bn * 128;
   const int kb = (K + 63) / 64;
   const int per = (kb + splits - 1) / splits;
@@ -483,12 +539,14 @@ static void gemm_smem_layout(int bn, int K, int splits, bool prefetch, int* stag
   // Long-K CTAs and split-K clusters (weight-streaming GEMMs of a few rows)
   // keep deep rings.
   const bool shallow = splits == 1 && per <= 12;
-  const int maxst = shallow ? (bn == 256 ? 2 : 3) : (bn == 256 ? 4 : (bn == 128 ? 6 : 8));
+  // (a direct epilogue stages nothing: two-stage rings of 64-wide and
+  // 128-wide tiles let three CTAs share an SM)
+  const int maxst = shallow ? (bn == 256 || direct ? 2 : 3) : (bn == 256 ? 4 : (bn == 128 ? 6 : 8));
   const int st = per < 2 ? 2 : (per > maxst ? maxst : per);
   const int ch = bn < 128 ? bn : 128;
   const int rpo = (128 + splits - 1) / splits;
   const int stg = splits * rpo * (ch + 4) * 4;
-  const int post = ((stg * (splits > 1 ? 2 : 1) + 1023) & ~1023) + (prefetch ? rpo * ch * 4 : 0);
+  const int post = direct ? 0 : ((stg * (splits > 1 ? 2 : 1) + 1023) & ~1023) + (prefetch ? rpo * ch * 4 : 0);
   int reg = st * stage > post ? st * stage : post;
   reg = (reg + 1023) & ~1023;
   *stages = st;
@@ -614,9 +672,19 @@ int gemm_plan(GemmPlan* g, const void* A, long long lda, long long a_gs, const v
   // chunk) when the output is a 16-byte-aligned f32 matrix.
   const int ch = bn < 128 ? bn : 128;
   const int rpo = (128 + splits - 1) / splits;
-  bool pf = (epi.epi == EPI_RESID || epi.epi == EPI_F32_ACCUM) && (epi.ldo % 4) == 0 && (N % 4) == 0 &&
-            (reinterpret_cast<uintptr_t>(epi.out) % 16) == 0 && (epi.out_gstride % 4) == 0;
-  gemm_smem_layout(bn, K, splits, pf, &g->p.stages, &g->p.region, &g->smem);
+  // Unsplit f16 tiles whose output rows take whole 16-column, 16-byte aligned
+  // segments write straight from the TMEM registers (no staging).
+  {
+    // (f16 outputs only: a residual read row by row costs more than the
+    // staged epilogue's TMA prefetch of it)
+    g->p.direct = splits == 1 && epi.epi == EPI_F16 && !epi.out32 && (N % 16) == 0 &&
+                  (epi.ldo % 8) == 0 && (epi.out_gstride % 8) == 0 &&
+                  (reinterpret_cast<uintptr_t>(epi.out) % 16) == 0 &&
+                  (!epi.bias || ((reinterpret_cast<uintptr_t>(epi.bias) % 16) == 0 && (epi.bias_gstride % 4) == 0));
+  }
+  bool pf = !g->p.direct && (epi.epi == EPI_RESID || epi.epi == EPI_F32_ACCUM) && (epi.ldo % 4) == 0 &&
+            (N % 4) == 0 && (reinterpret_cast<uintptr_t>(epi.out) % 16) == 0 && (epi.out_gstride % 4) == 0;
+  gemm_smem_layout(bn, K, splits, pf, &g->p.stages, &g->p.region, &g->smem, g->p.direct != 0);
   if (pf && g->smem > kMaxDynSmem) {
     pf = false;
     gemm_smem_layout(bn, K, splits, pf, &g->p.stages, &g->p.region, &g->smem);

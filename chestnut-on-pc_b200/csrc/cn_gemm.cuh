@@ -40,6 +40,7 @@ struct GemmParams {
   long long cond_ld;
   int rows_per_clip, tok_base, tok_gstride, T;
   int b_dep;          // 1: B may be written by an earlier kernel, so it is loaded only after griddepcontrol.wait
+  int direct;         // set by gemm_plan: unsplit tile, epilogue straight from the TMEM registers
 };
 
 struct GemmPlan {

@@ -83,6 +83,8 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// every store issued so far has read its shared-memory source
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 // Wait until at most n (< 4) copy groups of this thread are in flight.
 __device__ __forceinline__ void cp_async_wait_pending(int n) {
@@ -107,9 +109,21 @@ __device__ unsigned long long* g_stem_trace = nullptr;
     unsigned long long* tp_ = g_stem_trace;                                                           \
     if (tp_) tp_[(((size_t)(p)) * gridDim.x + blockIdx.x) * 16 + (k)] = global_ns();                 \
   } while (0)
+// Per-unit stamps of CTA 0 (its first 32 units of each phase), after the
+// per-CTA rows: [phase][unit ordinal][8 events].
+#define CN_SU(p, P, u, k)                                                                              \
+  do {                                                                                                \
+    unsigned long long* tp_ = g_stem_trace;                                                           \
+    const int j_ = ((u) - st_first(P)) / (int)gridDim.x;                                              \
+    if (tp_ && blockIdx.x == 0 && j_ < 32)                                                            \
+      tp_[(size_t)(kStemMaxPhases + 1) * gridDim.x * 16 + ((size_t)(p) * 32 + j_) * 8 + (k)] = global_ns(); \
+  } while (0)
 #else
 #define CN_ST(p, k) \
   do {              \
+  } while (0)
+#define CN_SU(p, P, u, k) \
+  do {                    \
   } while (0)
 #endif
 
@@ -229,12 +243,17 @@ __global__ void __launch_bounds__(kStThreads, 1)
   uint64_t* emptyW = bars + 4;   // [kStWStages]
   uint64_t* fullA = bars + 8;    // [kStAStages], two arrivals per phase
   uint64_t* emptyA = bars + 12;  // [kStAStages]
-  uint64_t* done = bars + 16;    // MMAs of a GEMM complete
   uint64_t* yready = bars + 17;  // fused 1x1 operand written
   uint64_t* redbar = bars + 18;  // reduction slices landed
   uint64_t* tfree = bars + 19;   // [2] accumulator half read out by the epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* flags = reinterpret_cast<volatile int*>(bars + 22);
+  // Per accumulator half, one phase per unit: the unit's GEMM MMAs complete
+  // (doneA), its fused 1x1 MMAs complete (doneB; right after doneA when the
+  // unit has none).  A half is reused only after the epilogue released it
+  // (tfree), so neither barrier can run two phases ahead of its waiter.
+  uint64_t* doneA = bars + 24;
+  uint64_t* doneB = bars + 26;
   uint8_t* ringA = smem + kStAOff;
   uint8_t* Y = smem + kStYOff;
   float* sbias = reinterpret_cast<float*>(smem + kStBiasOff);  // [0, 256) the GEMM's, [256, 384) the fused 1x1's
@@ -260,7 +279,10 @@ __global__ void __launch_bounds__(kStThreads, 1)
       mbar_init(&fullA[i], 2);  // two arrivals: the producer warps (cp.async) or the TMA issuer twice
       mbar_init(&emptyA[i], 1);
     }
-    mbar_init(done, 1);
+    mbar_init(&doneA[0], 1);
+    mbar_init(&doneA[1], 1);
+    mbar_init(&doneB[0], 1);
+    mbar_init(&doneB[1], 1);
     mbar_init(yready, 1);
     mbar_init(redbar, 1);
     mbar_init(&tfree[0], 1);
@@ -291,19 +313,18 @@ __global__ void __launch_bounds__(kStThreads, 1)
       // of this CTA is requested into L2 (the ring then reloads it from L2
       // whenever its phase comes).
       auto prefetch_rest = [&]() {
-        int n = 0;
+        // every CTA requests its 1/grid share of each phase's weights (units
+        // of many row tiles share theirs, so a per-unit walk would repeat)
         for (int p = 0; p < a.nph; ++p) {
           const StemPhase& P = sph[p];
-          const int BN = P.BN, N = P.N, KB1 = P.fuse ? P.KB1 : 0, units = P.units;
-          const uint8_t *w = P.w, *w1 = P.w1;
-          const long long w_gs = P.w_gs, w1_gs = P.w1_gs;
-          for (int u = st_first(P); u < units; u += gridDim.x) {
-            const SUnit U = st_unit(P, u);
-            for (int kb = U.kb0; kb < U.kb1; ++kb)
-              if (n++ >= 8)
-                bulk_prefetch_l2(w + U.g * w_gs + ((long long)kb * N + U.tn * BN) * 128, (uint32_t)BN * 128);
-            for (int kb = 0; kb < KB1; ++kb)
-              if (n++ >= 8) bulk_prefetch_l2(w1 + U.g * w1_gs + (long long)kb * N * 128, (uint32_t)N * 128);
+          for (int f = 0; f < (P.fuse ? 2 : 1); ++f) {
+            const long long R = (long long)(f ? P.KB1 : P.KB) * P.N * 128;  // one group's k-blocked tensor
+            const long long chunk = ((R + gridDim.x - 1) / gridDim.x + 255) / 256 * 256;
+            const long long off = (long long)blockIdx.x * chunk;
+            if (off >= R) continue;
+            const uint32_t bytes = (uint32_t)(R - off < chunk ? R - off : chunk);
+            for (int g = 0; g < P.G; ++g)
+              bulk_prefetch_l2((f ? P.w1 + g * P.w1_gs : P.w + g * P.w_gs) + off, bytes);
           }
         }
       };
@@ -312,7 +333,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
       for (int p = 0; p < a.nph && ok; ++p) {
         const StemPhase& P = sph[p];
         const int BN = P.BN, N = P.N, KB1 = P.fuse ? P.KB1 : 0, units = P.units;
-        const int kps = st_kps(BN), kps1 = st_kps(KB1 ? N : BN);
+        const int kps = P.kps, kps1 = P.kps1;
         const CUtensorMap* mw = &maps.w[p];
         const CUtensorMap* mw1 = &maps.w1[p];
         for (int u = st_first(P); u < units && ok; u += gridDim.x) {
@@ -356,8 +377,36 @@ __global__ void __launch_bounds__(kStThreads, 1)
       for (int p = 0; p < a.nph && ok; ++p) {
         const StemPhase& P = sph[p];
         const int units = P.units, KB1 = P.fuse ? P.KB1 : 0;
-        const int kps = st_kps(P.BN), kps1 = st_kps(KB1 ? P.N : P.BN), wsub = P.BN * 128, wsub1 = P.N * 128;
+        const int kps = P.kps, kps1 = P.kps1, wsub = P.BN * 128, wsub1 = P.N * 128;
+        const uint32_t yop = P.dec ? smem_u32(Y) : ring_a;  // the fused 1x1's operand
         const uint32_t idesc = umma_idesc_f16(P.BN, false), idesc1 = umma_idesc_f16(P.N, false);
+        const int n1 = KB1 ? (KB1 + kps1 - 1) / kps1 : 0;  // weight stages of a fused 1x1
+        const bool defer = P.defer != 0;
+        // The fused 1x1 of a unit into accumulator acc, its weight stages
+        // from ring index g1 on, once the epilogue has written its operand.
+        auto issue_1x1 = [&](uint32_t acc, uint32_t g1) -> bool {
+          if (!mbar_wait(yready, ny & 1, 44)) return false;
+          ++ny;
+          tc_fence_after();
+          for (int kb = 0, sub = 0; kb < KB1; ++kb) {
+            const int sw = (int)(g1 % kStWStages);
+            if (sub == 0 && !mbar_wait(&fullW[sw], (g1 / kStWStages) & 1, 45)) return false;
+            tc_fence_after();
+            const uint32_t ya = yop + kb * kStABytes, wa = ring_w + sw * kStWBytes + sub * wsub1;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              tc_mma_f16(acc, umma_desc_sw128(ya + 32 * k, 16, 1024), umma_desc_sw128(wa + 32 * k, 16, 1024), idesc1,
+                         (kb > 0 || k > 0) ? 1u : 0u);
+            if (++sub == kps1 || kb + 1 == KB1) {
+              tc_commit(&emptyW[sw]);
+              ++g1;
+              sub = 0;
+            }
+          }
+          return true;
+        };
+        bool pend1 = false;  // deferred: a unit whose 1x1 is still to be issued
+        uint32_t pacc = 0, pg1 = 0, plu = 0;
         for (int u = st_first(P); u < units && ok; u += gridDim.x, ++lu) {
           const SUnit U = st_unit(P, u);
           const uint32_t acc = tmem + 256u * (lu & 1);
@@ -375,7 +424,10 @@ __global__ void __launch_bounds__(kStThreads, 1)
               ok = false;
               break;
             }
-            if (kb == U.kb0) CN_ST(p, 5);
+            if (kb == U.kb0) {
+              CN_ST(p, 5);
+              CN_SU(p, P, u, 2);
+            }
             tc_fence_after();
             const uint32_t aa = ring_a + sa * kStABytes, wa = ring_w + sw * kStWBytes + sub * wsub;
 #pragma unroll
@@ -390,36 +442,41 @@ __global__ void __launch_bounds__(kStThreads, 1)
             }
           }
           if (!ok) break;
-          tc_commit(done);
+          tc_commit(&doneA[lu & 1]);
           CN_ST(p, 6);
-          if (KB1) {
-            if (!mbar_wait(yready, ny & 1, 44)) {
+          CN_SU(p, P, u, 3);
+          if (!KB1) {
+            tc_commit(&doneB[lu & 1]);
+          } else if (!defer) {
+            if (!issue_1x1(acc, gw)) {
               ok = false;
               break;
             }
-            ++ny;
-            tc_fence_after();
-            for (int kb = 0, sub = 0; kb < KB1; ++kb) {
-              const int sw = (int)(gw % kStWStages);
-              if (sub == 0 && !mbar_wait(&fullW[sw], (gw / kStWStages) & 1, 45)) {
+            gw += n1;
+            tc_commit(&doneB[lu & 1]);
+          } else {
+            // this unit's 1x1 waits for its operand while the next unit's
+            // GEMM is issued; the previous unit's 1x1 goes now
+            const uint32_t g1 = gw;
+            gw += n1;
+            if (pend1) {
+              if (!issue_1x1(pacc, pg1)) {
                 ok = false;
                 break;
               }
-              tc_fence_after();
-              const uint32_t ya = ring_a + kb * kStABytes, wa = ring_w + sw * kStWBytes + sub * wsub1;
-#pragma unroll
-              for (int k = 0; k < 4; ++k)
-                tc_mma_f16(acc, umma_desc_sw128(ya + 32 * k, 16, 1024), umma_desc_sw128(wa + 32 * k, 16, 1024),
-                           idesc1, (kb > 0 || k > 0) ? 1u : 0u);
-              if (++sub == kps1 || kb + 1 == KB1) {
-                tc_commit(&emptyW[sw]);
-                ++gw;
-                sub = 0;
-              }
+              tc_commit(&doneB[plu & 1]);
             }
-            if (!ok) break;
-            tc_commit(done);
+            pend1 = true;
+            pacc = acc;
+            pg1 = g1;
+            plu = lu;
           }
+        }
+        if (ok && pend1) {
+          if (issue_1x1(pacc, pg1))
+            tc_commit(&doneB[plu & 1]);
+          else
+            ok = false;
         }
       }
     }
@@ -429,17 +486,32 @@ __global__ void __launch_bounds__(kStThreads, 1)
     // Every phase field a loop uses is held in a register: the phase table is
     // in shared memory, which any global store could alias.
     const int ct = threadIdx.x - 64;
-    uint32_t ga = 0, nd = 0, nred = 0, lu = 0;
+    uint32_t ga = 0, nred = 0, lu = 0;
+    int bkey = -1;  // (phase, group, feature tile) whose bias columns are in sbias
+    // Decoupled units check the device error word once per unit; it is read
+    // one unit ahead, so the load's latency is hidden behind the unit's work.
+    int err_ahead = 0;
     bool ok = true;  // uniform over warps 2..7 (set from one verdict per unit)
     for (int p = 0; p < a.nph && ok; ++p) {
       const StemPhase& P = sph[p];
       const int units = P.units, S = P.S, BN = P.BN, N = P.N, Mg = P.Mg, rows_pad = P.rows_pad;
-      const int fuse = P.fuse, KB1 = P.KB1, epi = P.epi, dep0 = P.dep0, dep1 = P.dep1;
-      bool deps = false;
+      const int fuse = P.fuse, KB1 = P.KB1, epi = P.epi, dep0 = P.dep0, dep1 = P.dep1, dec = P.dec;
+      // the epilogue's staging: Y for decoupled units (the fused operand
+      // first, then the output), else the activation ring
+      uint8_t* const yop = dec ? Y : ringA;
+      uint8_t* const ystg = dec ? Y + (fuse ? kStABytes : 0) : ringA;
+      uint32_t pend = 0;  // decoupled: units done but not yet published
+      bool deps = false, edeps = false;
       for (int u = st_first(P); u < units && ok; u += gridDim.x, ++lu) {
         const SUnit U = st_unit(P, u);
         bool live = true;  // this thread's part of the unit proceeds (waits may expire)
         if (warp < 4) {
+          // decoupled: the loads run ahead of the epilogue and stop at a
+          // recorded error on their own (warp-uniform)
+          if (dec) {
+            if (__shfl_sync(0xffffffffu, err_ahead, 0)) break;
+            if (lane == 0) err_ahead = *reinterpret_cast<volatile int*>(&g_cn_dev_error);
+          }
           // ---------------- activation k-blocks: chunk i = (row i / 8, 16-byte column i % 8)
           if (!deps) {
             int met = 1;
@@ -471,7 +543,10 @@ __global__ void __launch_bounds__(kStThreads, 1)
                   live = false;
                   break;
                 }
-                if (i == 0) CN_ST(p, 14);
+                if (i == 0) {
+                  CN_ST(p, 14);
+                  CN_SU(p, P, u, 0);
+                }
                 const int k = (U.kb0 + i) * 64;
                 mbar_arrive_expect_tx(&fullA[sa], abytes);
                 mbar_arrive(&fullA[sa]);
@@ -484,6 +559,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
                 }
               }
               CN_ST(p, 2);
+              CN_SU(p, P, u, 1);
             }
             ga += nkb;
             __syncwarp();
@@ -536,7 +612,10 @@ __global__ void __launch_bounds__(kStThreads, 1)
                 }
               }
               const int kb = U.kb0 + issued;
-              if (kb == U.kb0 && threadIdx.x == 64) CN_ST(p, 14);
+              if (kb == U.kb0 && threadIdx.x == 64) {
+                CN_ST(p, 14);
+                CN_SU(p, P, u, 0);
+              }
               uint8_t* dst = ringA + sa * kStABytes;
               const int k = kb * 64 + j * 8;
               const bool kin = k < aK;
@@ -579,7 +658,10 @@ __global__ void __launch_bounds__(kStThreads, 1)
             if (lane == 0) mbar_arrive(&fullA[(ga + announced) % kStAStages]);
             ++announced;
           }
-          if (threadIdx.x == 64) CN_ST(p, 2);
+          if (threadIdx.x == 64) {
+            CN_ST(p, 2);
+            CN_SU(p, P, u, 1);
+          }
           cp_async_wait0();
           ga += nkb;
           }
@@ -592,20 +674,38 @@ __global__ void __launch_bounds__(kStThreads, 1)
           const uint32_t taddr = tmem + 256u * (lu & 1) + ((uint32_t)(32 * q) << 16);
           {
             // this unit's bias columns into shared memory while the MMAs run
-            // (the previous unit's readers are past the closing verdict)
+            // (the previous unit's readers are past its last barrier); units
+            // of the same group and feature tile keep what is there
             const int t = threadIdx.x - 128;
-            const float* b0 = P.bias + (long long)U.g * P.b_gs + U.tn * BN;
-            for (int i = t; i < BN; i += 128) sbias[i] = __ldg(b0 + i);
-            if (fuse) {
-              const float* b1 = P.bias1 + (long long)U.g * P.b1_gs;
-              for (int i = t; i < N; i += 128) sbias[256 + i] = __ldg(b1 + i);
+            const int key = ((p * 2 + U.g) << 8) + U.tn;
+            if (key != bkey) {
+              bkey = key;
+              const float* b0 = P.bias + (long long)U.g * P.b_gs + U.tn * BN;
+              for (int i = t; i < BN; i += 128) sbias[i] = __ldg(b0 + i);
+              if (fuse) {
+                const float* b1 = P.bias1 + (long long)U.g * P.b1_gs;
+                for (int i = t; i < N; i += 128) sbias[256 + i] = __ldg(b1 + i);
+              }
+            }
+            if (dec && threadIdx.x == 128) {
+              flags[0] = err_ahead != 0 ? 1 : 0;
+              err_ahead = *reinterpret_cast<volatile int*>(&g_cn_dev_error);
             }
             named_sync(kStBarEpi, 128);
-            if (threadIdx.x == 128) CN_ST(p, 15);
+            if (threadIdx.x == 128) {
+              CN_ST(p, 15);
+              CN_SU(p, P, u, 5);
+            }
           }
-          live = __all_sync(0xffffffffu, mbar_wait(done, nd & 1, 48));  // warp-uniform: tcgen05.ld is .aligned
-          ++nd;
-          if (threadIdx.x == 128) CN_ST(p, 7);
+          // decoupled: the epilogue stops at a recorded error on its own
+          // (uniform over its four warps: the flag was set before the barrier)
+          if (dec && flags[0]) break;
+          const uint32_t hpar = (lu >> 1) & 1;  // this unit's phase of its half's barriers
+          live = __all_sync(0xffffffffu, mbar_wait(&doneA[lu & 1], hpar, 48));  // warp-uniform: tcgen05.ld is .aligned
+          if (threadIdx.x == 128) {
+            CN_ST(p, 7);
+            CN_SU(p, P, u, 4);
+          }
           tc_fence_after();
           if (S == 1) {
             const int nout = fuse ? N : BN;
@@ -625,13 +725,13 @@ __global__ void __launch_bounds__(kStThreads, 1)
 #pragma unroll
                   for (int hh = 0; hh < 2; ++hh) {
                     const int c = c0 + 8 * hh, kb = c >> 6, jc = (c & 63) >> 3;
-                    *reinterpret_cast<uint4*>(ringA + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
+                    *reinterpret_cast<uint4*>(yop + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
                         *reinterpret_cast<const uint4*>(h + 8 * hh);
                   }
                 }
                 for (int c = N; c < KB1 * 64; c += 8) {
                   const int kb = c >> 6, jc = (c & 63) >> 3;
-                  *reinterpret_cast<uint4*>(ringA + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
+                  *reinterpret_cast<uint4*>(yop + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
                       make_uint4(0, 0, 0, 0);
                 }
               }
@@ -639,9 +739,11 @@ __global__ void __launch_bounds__(kStThreads, 1)
               tc_fence_before();
               named_sync(kStBarEpi, 128);
               if (threadIdx.x == 128) mbar_arrive(yready);
-              live = __all_sync(0xffffffffu, mbar_wait(done, nd & 1, 49)) && live;
-              ++nd;
-              if (threadIdx.x == 128) CN_ST(p, 8);
+              live = __all_sync(0xffffffffu, mbar_wait(&doneB[lu & 1], hpar, 49)) && live;
+              if (threadIdx.x == 128) {
+                CN_ST(p, 8);
+                CN_SU(p, P, u, 6);
+              }
               tc_fence_after();
             }
             // final accumulator -> output
@@ -661,7 +763,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
 #pragma unroll
                   for (int hh = 0; hh < 2; ++hh) {
                     const int c = c0 + 8 * hh, kb = c >> 6, jc = (c & 63) >> 3;
-                    *reinterpret_cast<uint4*>(ringA + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
+                    *reinterpret_cast<uint4*>(ystg + kb * kStABytes + row * 128 + ((jc ^ (row & 7)) << 4)) =
                         *reinterpret_cast<const uint4*>(h + 8 * hh);
                   }
                 }
@@ -673,13 +775,24 @@ __global__ void __launch_bounds__(kStThreads, 1)
                 if (live) {
                   const int col0 = fuse ? 0 : U.tn * BN;
                   for (int kb = 0; kb * 64 < nout; ++kb)
-                    tma_store_3d(&maps.o[p], ringA + kb * kStABytes, col0 + kb * 64, U.tm * 128, U.g);
+                    tma_store_3d(&maps.o[p], ystg + kb * kStABytes, col0 + kb * 64, U.tm * 128, U.g);
                   bulk_commit();
-                  bulk_wait_all();
-                  fence_proxy_async_global();
                 }
-                red_release_add(a.pctr + p, 1u);
+                if (dec) {
+                  // Y is free again once the store has read it; the rows are
+                  // published with the CTA's other units of the phase at its
+                  // end (the next phases wait for all units anyway)
+                  bulk_wait_read_all();
+                  ++pend;
+                } else {
+                  if (live) {
+                    bulk_wait_all();
+                    fence_proxy_async_global();
+                  }
+                  red_release_add(a.pctr + p, 1u);
+                }
                 CN_ST(p, 11);
+                CN_SU(p, P, u, 7);
               }
             } else {
               // f32 / token tiles (at most 64 features wide): the warps
@@ -700,11 +813,16 @@ __global__ void __launch_bounds__(kStThreads, 1)
                 }
               tc_fence_before();
               if (threadIdx.x == 128) {
-                // token tiles read the cond vector of this launch
+                // token tiles read the cond vector of this launch (waited
+                // for once per phase)
                 int met = 1;
-                if (dep0 >= 0) met = spin_until(a.pctr + dep0, (unsigned)sph[dep0].units * ep1, 52, ld_acquire_u32);
-                if (met && dep1 >= 0) met = spin_until(a.pctr + dep1, (unsigned)sph[dep1].units * ep1, 52, ld_acquire_u32);
-                fence_acq_rel_gpu();
+                if (!edeps) {
+                  if (dep0 >= 0) met = spin_until(a.pctr + dep0, (unsigned)sph[dep0].units * ep1, 52, ld_acquire_u32);
+                  if (met && dep1 >= 0)
+                    met = spin_until(a.pctr + dep1, (unsigned)sph[dep1].units * ep1, 52, ld_acquire_u32);
+                  fence_acq_rel_gpu();
+                  edeps = met != 0;
+                }
                 flags[2] = met;
               }
               named_sync(kStBarEpi, 128);
@@ -726,7 +844,10 @@ __global__ void __launch_bounds__(kStThreads, 1)
               fence_proxy_async_global();  // the next phases read these rows by TMA
               named_sync(kStBarEpi, 128);
               if (threadIdx.x == 128) {
-                red_release_add(a.pctr + p, 1u);
+                if (dec)
+                  ++pend;
+                else
+                  red_release_add(a.pctr + p, 1u);
                 CN_ST(p, 11);
               }
             }
@@ -807,12 +928,30 @@ __global__ void __launch_bounds__(kStThreads, 1)
             CN_ST(p, 11);
           }
         }
+        (void)live;
+        if (dec) continue;
         // one uniform verdict per unit for warps 2..7
         named_sync(kStBarRed, kStCompute);
         if (threadIdx.x == 64) flags[3] = !dev_error_set();
         named_sync(kStBarRed, kStCompute);
         ok = flags[3] != 0;
-        (void)live;
+      }
+      if (dec) {
+        // publish the last unit's rows; before a phase whose units may stage
+        // in the activation ring, one uniform verdict for warps 2..7 (that
+        // phase's loads start after it)
+        if (threadIdx.x == 128 && pend) {
+          bulk_wait_all();  // (no stores in flight for f32 / token phases)
+          fence_proxy_async_global();
+          red_release_add(a.pctr + p, pend);
+          pend = 0;
+        }
+        if (p + 1 < a.nph && !sph[p + 1].dec) {
+          named_sync(kStBarRed, kStCompute);
+          if (threadIdx.x == 64) flags[3] = !dev_error_set();
+          named_sync(kStBarRed, kStCompute);
+          ok = flags[3] != 0;
+        }
       }
     }
   }
@@ -926,6 +1065,23 @@ int stem_add(StemPlan* sp, const StemSpec& s) {
     return -1;
   }
   P.units = tiles * S;
+  // A ring stage holds one weight box of up to 32 KB, but no more k-blocks
+  // than the GEMM has (a short GEMM's box would be mostly zero fill).
+  P.kps = std::min(st_kps(P.BN), P.KB);
+  P.kps1 = fuse ? std::min(st_kps(s.N), (s.N + 63) / 64) : P.kps;
+  // Decoupled units: the epilogue stages the fused operand and the output in
+  // Y, off the activation ring, so the loads of the next units need not wait
+  // for it (a split's reduction and a wide fused operand use the ring).
+  P.dec = (S == 1 && (fuse ? s.N <= 64 : (s.epi != SE_RELU_F16 || P.BN <= 128))) ? 1 : 0;
+  // Deferred fused 1x1 (decoupled units only: the next unit's loads must not
+  // wait for this unit's epilogue): the MMA thread issues unit u + 1's GEMM
+  // before unit u's 1x1, consuming weight stages out of order, which needs
+  // both of a unit's weight streams in the ring at once.
+  {
+    const int KB1 = (s.N + 63) / 64;
+    const int n3 = (P.KB + P.kps - 1) / P.kps, n1 = (KB1 + P.kps1 - 1) / P.kps1;
+    P.defer = (P.dec && fuse && n3 + n1 <= kStWStages) ? 1 : 0;
+  }
   P.cta0 = sp->next_cta % sp->grid;
   sp->next_cta += P.units;
   P.akind = s.akind;
@@ -1000,7 +1156,7 @@ int stem_plan_end(StemPlan* sp, float* part, void* counters) {
       const uint64_t d[4] = {64, (uint64_t)P.N, (uint64_t)P.KB, (uint64_t)P.G};
       const uint64_t st[3] = {128, (uint64_t)P.N * 128,
                               (uint64_t)(P.G > 1 ? P.w_gs : (long long)P.KB * P.N * 128)};
-      const uint32_t box[4] = {64, (uint32_t)P.BN, (uint32_t)st_kps(P.BN), 1};
+      const uint32_t box[4] = {64, (uint32_t)P.BN, (uint32_t)P.kps, 1};
       if (encode(&sp->maps.w[p], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, P.w, d, st, box, CU_TENSOR_MAP_SWIZZLE_128B))
         return -3;
     }
@@ -1034,7 +1190,7 @@ int stem_plan_end(StemPlan* sp, float* part, void* counters) {
       const uint64_t d[4] = {64, (uint64_t)P.N, (uint64_t)P.KB1, (uint64_t)P.G};
       const uint64_t st[3] = {128, (uint64_t)P.N * 128,
                               (uint64_t)(P.G > 1 ? P.w1_gs : (long long)P.KB1 * P.N * 128)};
-      const uint32_t box[4] = {64, (uint32_t)P.N, (uint32_t)st_kps(P.N), 1};
+      const uint32_t box[4] = {64, (uint32_t)P.N, (uint32_t)P.kps1, 1};
       if (encode(&sp->maps.w1[p], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, P.w1, d, st, box, CU_TENSOR_MAP_SWIZZLE_128B))
         return -3;
     }

@@ -56,6 +56,9 @@ struct StemPhase {
   long long lda, a_gs;
   int Hin, Win, Cin, Ho, Wo;
   int lHin, lWin, lCin, lHo, lWo;  // SA_GATHER: log2 of the (power-of-two) extents
+  int kps, kps1;                   // weight k-blocks per ring stage (GEMM, fused 1x1)
+  int dec;                         // 1: loads run ahead of the epilogue (it stages in Y only)
+  int defer;                       // 1: a unit's fused 1x1 is issued after the next unit's GEMM
   int atma;                        // 1: activation k-blocks by TMA (else 16-byte cp.async)
   int abytes;                      // bytes one activation TMA box lands
   int B;                           // images per group (SA_GATHER)
