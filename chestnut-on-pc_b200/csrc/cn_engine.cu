@@ -159,7 +159,7 @@ struct cn_engine {
   __half* h2 = nullptr;  // LN2 output of the persistent trunk
   uint8_t* tctr = nullptr;
   size_t tctr_bytes = 0;
-  // persistent conv stem (single-clip frames): split-K partials + counters
+  // persistent conv stem: split-K partials + counters
   bool use_stem = false;
   StemPlan stem;
   float* spart = nullptr;
@@ -263,8 +263,8 @@ static size_t cam_stride_bytes(cn_engine* e, const std::string& cam0name) {
   return (size_t)((uint8_t*)wptr(e, other) - (uint8_t*)wptr(e, cam0name));
 }
 
-// The conv stem, the cond embedding and the token embeddings of a single-clip
-// frame as the phases of one persistent launch (cn_stem.cu).  Phase order:
+// The conv stem, the cond embedding and the token embeddings of a frame (one
+// clip or a batch) as the phases of one persistent launch (cn_stem.cu).  Phase order:
 // stage 0 (3x3 + fused 1x1), cond, temporal tokens, stage 1, then the other
 // stages (the 1x1 fused while the stage has at most 256 channels), then the
 // visual tokens.

@@ -1,4 +1,4 @@
-// Persistent conv stem and token embeddings for single-clip frames.
+// Persistent conv stem and token embeddings (one clip or a batch of clips).
 //
 // The conv stem of a frame (compile_modeld.py's vision encoder as restated in
 // the synthetic layer list: per camera five 3x3 / stride-2 convs, each with a
