@@ -484,7 +484,7 @@ def run_ours(args, rank, world, local_rank):
         eng.sync()
         kms += eng.timed_class_ms()
     eng.set_timed_class("")
-    # the persistent conv stem (single-clip frames), timed the same way
+    # the persistent conv stem, timed the same way
     stem_ms = None
     if any(k["name"] == "conv_stem" for k in eng.kernel_list()):
         eng.set_timed_class("conv_stem")
