@@ -357,6 +357,43 @@ def bench_frame(model, dev=0, frames=300, warmup=10):
                          "weight_bytes": info["weight_bytes"], "flops": fl, "frac": floor / p50, "peak_source": src}}
 
 
+def bench_clip_step(B=64, dev=0, steps=50, warmup=5):
+    """One config-5 frame step of B batched 39M clips: device-resident inputs,
+    one graph replay per step (CUDA events on the engine's stream), then one
+    eager frame with per-launch device times (serialised, so shares only)."""
+    import torch
+    from chestnut_b200 import DeviceBuffer, Engine
+    eng = Engine("39m", device=dev, batch=B, seed=0, carry_hidden=True)
+    stream = torch.cuda.ExternalStream(eng.stream_handle(), device=dev)
+    rng = np.random.default_rng(5)
+    w = rng.integers(0, 256, (B, 2, 6, 128, 256), dtype=np.uint8)
+    pk = np.zeros((B, 524), np.float32)
+    pk[:, 8] = 1.0
+    dW, dP = DeviceBuffer(w.nbytes, dev).upload(w), DeviceBuffer(pk.nbytes, dev).upload(pk)
+    for _ in range(warmup):
+        eng.run_frame_device(dW.ptr, dP.ptr)
+    eng.sync()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        eng.run_frame_device(dW.ptr, dP.ptr)
+    b.record(stream)
+    eng.sync()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / steps
+    prof = eng.profile_frame(w, pk)
+    eng.close()
+    tot = sum(t for _, t in prof)
+    kinds = {}
+    for name, t in prof:
+        k = name.split(":")[0]
+        kinds[k] = kinds.get(k, 0.0) + t
+    return {"kernel": f"config-5 frame step, {B} batched 39M clips", "ms_per_step": ms, "frames_per_s": B / ms * 1e3,
+            "launches": len(prof),
+            "eager_launch_list": [{"name": n, "us": round(t * 1e3, 1), "share": round(t / tot, 4)} for n, t in prof],
+            "by_kind_share": {k: round(v / tot, 4) for k, v in sorted(kinds.items(), key=lambda x: -x[1])}}
+
+
 def cpu_kernel_baselines():
     """Configs 1 and 2 on the host cores through the C restatement (oracle/cref.c,
     OpenMP, every thread), and config 3 through the numpy oracle frame."""
@@ -771,7 +808,7 @@ def main():
     ap.add_argument("--clip-frames", type=int, default=1200, help="frames per clip in the clip-throughput leg")
     ap.add_argument("--clip-batch", type=int, default=0,
                     help="clips per launch in the clip-throughput leg (0: all of a rank's clips, at most 64)")
-    ap.add_argument("--kernel", choices=["gemm", "reduce", "frame39m", "warp"],
+    ap.add_argument("--kernel", choices=["gemm", "reduce", "frame39m", "warp", "clips39m"],
                     help="run one kernel-level leg alone and print its JSON")
     ap.add_argument("--bn", type=int, default=0)
     ap.add_argument("--splits", type=int, default=0)
@@ -791,6 +828,8 @@ def main():
             line = bench_reduce(args.reps or 10, rows=args.reduce_rows)
         elif args.kernel == "warp":
             line = bench_warp(args.reps or 64)
+        elif args.kernel == "clips39m":
+            line = bench_clip_step(args.clip_batch or 64, local_rank)
         else:
             line = bench_frame("39m", local_rank)
     elif args.impl == "reference":
