@@ -10,35 +10,46 @@
 //
 //   warp 0 (lane 0)  streams the weight k-blocks of every unit this CTA will
 //                    run, over all phases, into a ring of three 32 KB stages
-//                    with TMA (one box of 1-4 k-blocks per stage; the weights
+//                    with TMA (one box of 1-8 k-blocks per stage; the weights
 //                    never depend on the frame, so they are in flight while
-//                    earlier phases compute); what does not fit in the ring
-//                    is requested into L2 at launch.
+//                    earlier phases compute); each CTA also requests its
+//                    1/grid share of every phase's weights into L2 at launch.
 //   warp 1 (lane 0)  issues tcgen05.mma (M = 128 rows, N = the tile's
-//                    features, f32 accumulators in TMEM).
-//   warps 2, 3       build the activation k-blocks in shared memory with
-//                    16-byte cp.async copies in the 128-byte-swizzled layout
-//                    the MMA reads.  A 3x3 conv's operand is gathered straight
-//                    from the previous stage's NHWC output (zero border by
-//                    zero-fill copies), so no im2col matrix is written.
+//                    features, f32 accumulators in TMEM, units alternating
+//                    between the two 256-column halves).
+//   warps 2, 3       load the activation k-blocks into a 4-slot ring in the
+//                    128-byte-swizzled layout the MMA reads: TMA boxes for
+//                    row operands and for a 3x3 conv over 64-channel input
+//                    (a strided box over the previous stage's NHWC output,
+//                    the zero border as its out-of-bounds fill), else 16-byte
+//                    cp.async gathers with zero-fill at the border.  No im2col
+//                    matrix is written.
 //   warps 4..7       epilogue from TMEM (lane quadrant = warp & 3).
 //   warps 2..7       the split-K reduction.
 //
 // A phase is one GEMM cut into units (group, 128-row tile, feature tile,
 // split).  Phases meet on dataflow counters: a unit's activation loads wait
-// only for the phases it reads, and a unit publishes its completion with a
-// release add.  Split-K units store their partials ([feature][row], so a
-// warp's stores are whole 128-byte lines), meet on a per-tile arrival
-// counter, and then each reduces a band of 8-feature column groups: its
-// slices of all S partials arrive by bulk copies into shared memory and are
-// added in split order 0..S-1 (deterministic).  The first two stages fuse the
-// 1x1 conv into the 3x3 unit: the ReLU output goes to shared memory as the
-// next MMA's operand and never leaves the SM.
+// only for the phases it reads, and completions are published with release
+// adds.  Split-K units store their partials ([feature][row], so a warp's
+// stores are whole 128-byte lines), meet on a per-tile arrival counter, and
+// then each reduces a band of 8-feature column groups: its slices of all S
+// partials arrive by bulk copies into shared memory and are added in split
+// order 0..S-1 (deterministic).  Stages of at most 256 channels fuse the 1x1
+// conv into the 3x3 unit: the ReLU output goes to shared memory as the next
+// MMA's operand and never leaves the SM.
+//
+// Decoupled phases (unsplit units whose epilogue stages only in the Y buffer:
+// a fused operand of one k-block, an output of at most two 64-column boxes,
+// or f32 / token rows) let the loads run ahead of the epilogue; warps 2..3
+// and 4..7 then meet once per phase and publish once per phase, and a unit's
+// fused 1x1 is issued after the next unit's 3x3 where both weight streams fit
+// in the ring together.  Batched clips (tens of units per CTA and phase) live
+// on this; other phases run unit by unit in lock-step.
 //
 // Every wait is bounded (%globaltimer); on timeout a code lands in the device
 // error word and the roles unwind (named barriers are always reached by every
-// warp of their group).  Counters are monotonic across launches.  No TMA
-// multicast.
+// warp of their group).  Counters are monotonic across launches (compared
+// wrap-safe).  No TMA multicast.
 #include <algorithm>
 
 #include "cn_common.cuh"
